@@ -1,0 +1,142 @@
+/*
+ * kllm_cuda.h -- extensions of the kllm C ABI that the B200 executor adds
+ * next to the drop-in surface of tape_runner.h.
+ *
+ * None of these exists in the reference runtime (csrc/tape_runner.h); each
+ * comment says which reference behaviour it complements.  All functions are
+ * plain C: pointers and sizes only.
+ */
+#ifndef KLLM_CUDA_H
+#define KLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tape_runner.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- errors --
+ * The reference has no error reporting (void functions, exit(1) in the
+ * loaders, processor_infer* always return 0: _tape_runner.c:1587,1762).
+ * Here every failure is recorded per thread and the call returns. */
+
+/* Message of the first error recorded on this thread since the last clear,
+ * or NULL when there is none. */
+const char *kllm_last_error(void);
+void kllm_clear_error(void);
+
+/* Version string of this library. */
+const char *kllm_version(void);
+
+/* Number of CUDA devices visible to this process (0 without a GPU). */
+int kllm_device_count(void);
+
+/* Device used by contexts created afterwards on this thread (default: the
+ * CUDA current device).  Returns 0, or -1 for an invalid ordinal. */
+int kllm_set_device(int device);
+
+/* tape_run with a status: 0 on success, non-zero on error
+ * (complements _tape_runner.c:665, which cannot fail). */
+int kllm_tape_run(TapeCtx *ctx);
+
+/* Kernels launched by this process so far (all contexts). */
+long long kllm_launch_count(void);
+
+/* --------------------------------------------------- inference options --
+ * processor_infer / processor_infer_bytes keep the reference signatures;
+ * these settings ride on the context. */
+enum {
+    KLLM_MODE_AUTO = 0,     /* fused decode plan when the tape matches the
+                               compiler's LLaMA template, else per-op */
+    KLLM_MODE_GENERIC = 1,  /* per-op device execution of every instruction
+                               (same loop structure as the reference) */
+    KLLM_MODE_FUSED = 2     /* fused plan or an error */
+};
+
+typedef struct {
+    int mode;                /* KLLM_MODE_* */
+    float *logits_out;       /* optional host buffer: the logits row after
+                                every tape step, [logits_rows][vocab] */
+    int logits_rows;         /* capacity of logits_out in rows */
+    int use_graphs;          /* replay each step as a CUDA graph (fused) */
+    int reserved[8];
+} kllm_infer_opts;
+
+typedef struct {
+    int fused;               /* 1 when the fused plan ran */
+    int steps;               /* tape steps run (prompt + generated) */
+    double prefill_ms;       /* device time of the prompt steps */
+    double decode_ms;        /* device time of the generation steps */
+    double total_ms;         /* wall time inside the call */
+    long long launches;      /* kernels launched inside the call */
+    int reserved[8];
+} kllm_infer_stats;
+
+void kllm_default_infer_opts(kllm_infer_opts *o);
+int kllm_set_infer_opts(TapeCtx *ctx, const kllm_infer_opts *o);
+int kllm_get_infer_stats(TapeCtx *ctx, kllm_infer_stats *s);
+
+/* ----------------------------------------------------------- TT-GEMV -----
+ * y[r][n] = sum_k fl(x[r][k] * codebook[idx[k][n]]) in the accumulation
+ * order of the reference TT-GEMV (_tape_runner.c:495-663): K is cut into
+ * T = min(8, ceil(K/128)) chunks (the first K%T chunks one row longer),
+ * each chunk is summed row by row from 0.0f, and the chunk sums are added
+ * in chunk order.  Results are bit-identical to the reference for every
+ * input.  idx is uint16 row-major [K][N]; codebook has n_codes floats.
+ *
+ * Device-pointer form: all pointers are device memory of the calling
+ * thread's device; stream is a cudaStream_t (NULL = default stream).  Uses
+ * a per-device scratch buffer for the chunk partials, grown on demand with
+ * cudaMalloc.  Returns 0 or non-zero on error (see kllm_last_error). */
+int kllm_tt_gemv(const float *x, int rows, const float *codebook, int n_codes,
+                 const uint16_t *idx, int K, int N, float *y, void *stream);
+
+/* Host-buffer form of the same product: copies x, codebook and idx to the
+ * device, runs, copies y back (synchronous). */
+int kllm_tt_gemv_host(const float *x, int rows, const float *codebook,
+                      int n_codes, const uint16_t *idx, int K, int N, float *y);
+
+/* ------------------------------------------------------------- chips -----
+ * Chip directory loader: the same files, read the same way, as the
+ * reference CLI's static chip_load (csrc/kllm.c:152-388): processor.json,
+ * tables/*.bin, bpe/*, circuit/tape.bin + slots.bin + const_<slot>*.bin.
+ * The loader validates what the reference trusts (file sizes against
+ * slots.bin, the 276-byte record size, slot ids in processor.json) and
+ * returns NULL with kllm_last_error() set instead of exiting. */
+typedef struct kllm_chip kllm_chip;
+
+kllm_chip *kllm_chip_open(const char *chip_dir);
+void kllm_chip_close(kllm_chip *chip);
+TapeCtx *kllm_chip_ctx(kllm_chip *chip);
+
+/* info[0..17] = vocab_size, hidden_dim, num_layers, num_kv_heads, head_dim,
+ * max_seq_len, eos_token_id, logits_slot, token_embed_slot, rope_cos_slot,
+ * rope_sin_slot, n_slots, n_instrs, bos_token_id, hash table_size,
+ * max_piece_len, num_merges, num_special. */
+int kllm_chip_info(kllm_chip *chip, int *info);
+
+/* processor_infer with the chip's tables and slot maps (what kllm.c passes,
+ * csrc/kllm.c:566-584, minus the BPE). */
+int kllm_chip_infer(kllm_chip *chip, const int *prompt, int prompt_len, int max_new,
+                    int eos_token_id, int *out_tokens, int *out_len);
+
+/* processor_infer_bytes with the chip's ROMs, as `kllm infer` calls it
+ * (csrc/kllm.c:566-584); max_seq_tokens <= 0 means the chip's max_seq_len. */
+int kllm_chip_infer_bytes(kllm_chip *chip, const uint8_t *input, int input_len, int max_new,
+                          int max_seq_tokens, token_callback_fn cb, void *user_data,
+                          int *total_generated);
+
+/* bpe_encode / bpe_decode with the chip's ROMs. */
+int kllm_chip_encode(kllm_chip *chip, const uint8_t *bytes, int len, int max_tokens,
+                     int32_t *out_ids);
+int kllm_chip_decode(kllm_chip *chip, const int32_t *ids, int n, int max_bytes,
+                     int skip_leading_space, uint8_t *out_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLLM_CUDA_H */

@@ -1,0 +1,32 @@
+// plan.cuh -- fused decode plan for the compiler's LLaMA decode template.
+#pragma once
+
+#include <functional>
+#include <string>
+
+#include "common.cuh"
+
+namespace kllm {
+
+// What processor_infer knows about the chip (its arguments).
+struct PlanDesc {
+    const float *embed = nullptr;
+    int vocab = 0, hidden = 0;
+    const float *rope_cos = nullptr, *rope_sin = nullptr;
+    int head_dim = 0;
+    int embed_slot = -1, cos_slot = -1, sin_slot = -1;
+    const int *kv_in = nullptr, *kv_out = nullptr;
+    int logits_slot = -1, n_layers = 0, n_kv = 0;
+};
+
+// Match the tape against the template and stage the plan's device state
+// (weights, KV cache for max_pos positions, graphs).  Returns false with a
+// reason when the tape is not the template; no error is recorded then.
+bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why);
+
+// Prefill + greedy decode on the plan.  emit(token, i) is called for every
+// generated token in order and returns false to stop.
+bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,
+                int eos, const std::function<bool(int, int)> &emit, int *generated);
+
+}  // namespace kllm

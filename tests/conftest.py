@@ -1,0 +1,83 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path.insert(0, HERE)
+sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); runs the product kernels")
+    config.addinivalue_line("markers", "slow: full-size model runs (minutes)")
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    import harness
+    return harness.Oracle()
+
+
+@pytest.fixture(scope="session")
+def ref():
+    import harness
+    if not harness.have_ref():
+        pytest.skip("reference build oracle/_ref not present")
+    return harness.Ref()
+
+
+@pytest.fixture(scope="session")
+def gpu():
+    import harness
+    import kmap_b200
+    kmap_b200.lib()
+    if kmap_b200.device_count() < 1:
+        pytest.fail("GPU test without a visible CUDA device")
+    return harness.Gpu()
+
+
+@pytest.fixture(scope="session")
+def built_lib():
+    """libkllm_cuda.so, built if missing (loads without a GPU)."""
+    import kmap_b200
+    from kmap_b200 import build
+    if not os.path.exists(kmap_b200.LIB_PATH):
+        build.build()
+    return kmap_b200.lib()
+
+
+TINY_SPECS = {
+    # GQA (groups = 2), random norm weights
+    "gqa": dict(num_layers=2, hidden_size=128, num_attention_heads=4, num_key_value_heads=2,
+                intermediate_size=256, vocab_size=600, max_seq=64, norm_weights="random"),
+    # MHA (no REPEAT in the tape), odd-ish sizes
+    "mha": dict(num_layers=3, hidden_size=192, num_attention_heads=3, num_key_value_heads=3,
+                intermediate_size=320, vocab_size=777, max_seq=96, norm_weights="random",
+                seed=5),
+    # TinyLlama's head geometry (hd 64, 8 q heads per kv head) at a small width
+    "tl": dict(num_layers=2, hidden_size=512, num_attention_heads=8, num_key_value_heads=1,
+               intermediate_size=1408, vocab_size=2048, max_seq=160, seed=7),
+}
+
+
+@pytest.fixture(scope="session")
+def chip_dir(tmp_path_factory):
+    """Directory holding generated tiny chips (built on first use)."""
+    from kmap_b200 import chipgen
+    root = tmp_path_factory.mktemp("chips")
+    made = {}
+
+    def get(name):
+        if name not in made:
+            spec = chipgen.ModelSpec(**TINY_SPECS[name])
+            made[name] = chipgen.ensure_chip(str(root), spec)
+        return made[name]
+    return get
+
+
+@pytest.fixture
+def rng():
+    return np.random.default_rng(1234)

@@ -1,0 +1,82 @@
+"""End-to-end generation on the device (needs a B200).
+
+Bar (the north star's): greedy token IDs identical to the reference /
+oracle, logits within max-abs 1e-3 and rel 1e-4 (np.allclose with
+atol=1e-3, rtol=1e-4)."""
+import numpy as np
+import pytest
+
+import harness
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-3, 1e-4
+
+
+def _oracle_run(oracle, path, prompt, max_new):
+    oc = harness.OracleChip(oracle, path)
+    toks, lg = oc.infer(prompt, max_new)
+    oc.close()
+    return toks, lg
+
+
+@pytest.mark.parametrize("name", ["gqa", "mha", "tl"])
+@pytest.mark.parametrize("mode", ["generic", "auto"])
+def test_tiny_chip_tokens_and_logits(gpu, oracle, chip_dir, name, mode):
+    import kmap_b200
+    path = chip_dir(name)
+    with kmap_b200.Chip(path) as chip:
+        V = chip.info["vocab_size"]
+        prompt = np.random.default_rng(11).integers(3, V, 7)
+        max_new = 20
+        toks_o, lg_o = _oracle_run(oracle, path, prompt, max_new)
+        m = kmap_b200.MODE_GENERIC if mode == "generic" else kmap_b200.MODE_AUTO
+        toks_g, lg_g = chip.infer(prompt, max_new, mode=m, logits=True)
+        assert toks_g.tolist() == toks_o.tolist()
+        np.testing.assert_allclose(lg_g, lg_o, rtol=RTOL, atol=ATOL)
+
+
+def test_eos_stops_generation(gpu, oracle, chip_dir):
+    import kmap_b200
+    path = chip_dir("gqa")
+    with kmap_b200.Chip(path) as chip:
+        prompt = np.array([5, 9, 13], np.int32)
+        full = chip.infer(prompt, 12)
+        eos = int(full[4])
+        first = int(np.nonzero(full == eos)[0][0])
+        cut = chip.infer(prompt, 12, eos=eos)
+        assert cut.tolist() == full[:first].tolist()
+
+
+def test_golden_tiny_decode_on_gpu(gpu, tmp_path):
+    import os
+
+    import kmap_b200
+    from kmap_b200 import chipgen
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                             "tiny_decode.npz"))
+    spec = chipgen.ModelSpec(**dict(zip(g["spec_keys"].tolist(), g["spec_vals"].tolist())))
+    for k in ("num_layers", "hidden_size", "num_attention_heads", "num_key_value_heads",
+              "intermediate_size", "vocab_size", "max_seq", "seed"):
+        setattr(spec, k, int(getattr(spec, k)))
+    path = chipgen.ensure_chip(str(tmp_path), spec)
+    with kmap_b200.Chip(path) as chip:
+        toks, lg = chip.infer(g["prompt"], int(g["max_new"]), logits=True)
+    assert toks.tolist() == g["tokens"].tolist()
+    np.testing.assert_allclose(lg, g["logits"], rtol=RTOL, atol=ATOL)
+
+
+def test_infer_bytes_matches_reference(gpu, ref, chip_dir):
+    import kmap_b200
+    path = chip_dir("tl")
+    h, info = ref.chip(path)
+    text = b"<|user|>\nWhat is the capital of France?</s>\n<|assistant|>\n"
+    out_r, gen_r = ref.infer_bytes(h, text, 12, int(info[5]))
+    ref.L.refh_chip_destroy(h)
+    with kmap_b200.Chip(path) as chip:
+        out_g, gen_g, pieces = chip.infer_bytes(text, 12)
+        assert gen_g == gen_r
+        assert out_g == out_r
+        # a callback that asks to stop ends generation after that token
+        out_s, gen_s, _ = chip.infer_bytes(text, 12, stop_after=3)
+        assert gen_s == 3 and out_s == b"".join(pieces[:3])
