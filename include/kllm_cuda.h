@@ -79,6 +79,16 @@ void kllm_default_infer_opts(kllm_infer_opts *o);
 int kllm_set_infer_opts(TapeCtx *ctx, const kllm_infer_opts *o);
 int kllm_get_infer_stats(TapeCtx *ctx, kllm_infer_stats *s);
 
+/* Whether processor_infer takes the fused decode plan for this tape: 1
+ * when the tape is the kllm compiler's LLaMA decode template
+ * (kllm_compile.c:1143-1385) for these dimensions and slot maps, 0 when not
+ * (the first mismatch is written to why), -1 on bad arguments.  Host only;
+ * needs no GPU. */
+int kllm_plan_match(TapeCtx *ctx, int vocab_size, int hidden_dim, int head_dim,
+                    int token_embed_slot, int rope_cos_slot, int rope_sin_slot,
+                    const int *kv_in_slots, const int *kv_out_slots, int logits_slot,
+                    int n_layers, int num_kv_heads, char *why, int why_len);
+
 /* ----------------------------------------------------------- TT-GEMV -----
  * y[r][n] = sum_k fl(x[r][k] * codebook[idx[k][n]]) in the accumulation
  * order of the reference TT-GEMV (_tape_runner.c:495-663): K is cut into
@@ -88,14 +98,16 @@ int kllm_get_infer_stats(TapeCtx *ctx, kllm_infer_stats *s);
  * input.  idx is uint16 row-major [K][N]; codebook has n_codes floats.
  *
  * Device-pointer form: all pointers are device memory of the calling
- * thread's device; stream is a cudaStream_t (NULL = default stream).  Uses
- * a per-device scratch buffer for the chunk partials, grown on demand with
- * cudaMalloc.  Returns 0 or non-zero on error (see kllm_last_error). */
+ * thread's device; stream is a cudaStream_t (NULL = default stream).  Every
+ * index must be < n_codes (not checked here: the caller owns the data).
+ * Uses a per-device scratch buffer for the chunk partials, grown on demand
+ * with cudaMalloc.  Returns 0 or non-zero on error (see kllm_last_error). */
 int kllm_tt_gemv(const float *x, int rows, const float *codebook, int n_codes,
                  const uint16_t *idx, int K, int N, float *y, void *stream);
 
-/* Host-buffer form of the same product: copies x, codebook and idx to the
- * device, runs, copies y back (synchronous). */
+/* Host-buffer form of the same product: checks every index against
+ * n_codes, copies x, codebook and idx to the device, runs, copies y back
+ * (synchronous). */
 int kllm_tt_gemv_host(const float *x, int rows, const float *codebook,
                       int n_codes, const uint16_t *idx, int K, int N, float *y);
 

@@ -53,6 +53,9 @@ _SIGS = {
     "kllm_chip_encode": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_int, _fp(C.c_int32)]),
     "kllm_chip_decode": (C.c_int, [C.c_void_p, _fp(C.c_int32), C.c_int, C.c_int, C.c_int,
                                     C.c_char_p]),
+    "kllm_plan_match": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, _fp(C.c_int), _fp(C.c_int), C.c_int, C.c_int,
+                                  C.c_int, C.c_char_p, C.c_int]),
     "tape_ctx_create": (C.c_void_p, [C.c_int, C.c_int]),
     "tape_ctx_destroy": (None, [C.c_void_p]),
     "tape_ctx_n_instrs": (C.c_int, [C.c_void_p]),
@@ -213,6 +216,25 @@ class Chip:
             o.logits_out = logits.ctypes.data
             o.logits_rows = logits.shape[0]
         check(lib().kllm_set_infer_opts(self.ctx, C.byref(o)), "kllm_set_infer_opts")
+
+    def plan_match(self, kv_in=None, kv_out=None):
+        """(matched, reason): whether processor_infer takes the fused plan."""
+        import json
+        m = json.load(open(os.path.join(self.path, "processor.json")))
+        L = m["num_layers"]
+        if kv_in is None:
+            kv_in = [m["input_map"]["L%d/cache_%s" % (l, c)] for l in range(L) for c in "kv"]
+        if kv_out is None:
+            kv_out = [m["output_map"]["L%d/new_%s" % (l, c)] for l in range(L) for c in "kv"]
+        ki = np.asarray(kv_in, np.int32)
+        ko = np.asarray(kv_out, np.int32)
+        why = C.create_string_buffer(512)
+        i = self.info
+        r = lib().kllm_plan_match(self.ctx, i["vocab_size"], i["hidden_dim"], i["head_dim"],
+                                  i["token_embed_slot"], i["rope_cos_slot"], i["rope_sin_slot"],
+                                  _iptr(ki), _iptr(ko), i["logits_slot"], i["num_layers"],
+                                  i["num_kv_heads"], why, 512)
+        return r == 1, why.value.decode()
 
     def stats(self) -> dict:
         s = InferStats()

@@ -696,3 +696,28 @@ def ensure_chip(cache_root: str, spec: ModelSpec, log=None) -> str:
         generate_chip(path, spec, log=log)
         open(done, "w").close()
     return path
+
+
+# ------------------------------------------------------ TT-GEMV inputs --
+
+def gaussian_rank_indices(rng, K, N, n_codes, sigma=0.02, codebook=None):
+    """uint16 indices whose code frequencies follow the Gaussian rank that
+    bf16-rounding N(0, sigma) produces: draw w ~ N(0, sigma) and take the
+    nearest entry of the sorted codebook."""
+    if n_codes == 1:
+        return np.zeros((K, N), np.uint16)
+    w = rng.standard_normal((K, N), dtype=np.float32) * np.float32(sigma)
+    pos = np.clip(np.searchsorted(codebook, w), 1, n_codes - 1)
+    left, right = codebook[pos - 1], codebook[pos]
+    pick = np.where(np.abs(w - left) <= np.abs(right - w), pos - 1, pos)
+    return pick.astype(np.uint16)
+
+
+def tt_case(seed, K, N, n_codes, rows=1):
+    """A TT-GEMV microbenchmark input: sorted seeded N(0, 0.02) codebook of
+    n_codes entries, Gaussian-rank uint16 indices [K][N], x ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    cb = np.sort(rng.standard_normal(n_codes).astype(np.float32) * np.float32(0.02))
+    idx = gaussian_rank_indices(rng, K, N, n_codes, codebook=cb)
+    x = rng.standard_normal((rows, K), dtype=np.float32)
+    return x, cb, idx

@@ -292,3 +292,31 @@ extern "C" int processor_infer_bytes(
     *total_generated = gen;
     return ok ? 0 : -1;
 }
+
+extern "C" int kllm_plan_match(TapeCtx *ctx, int vocab_size, int hidden_dim, int head_dim,
+                               int token_embed_slot, int rope_cos_slot, int rope_sin_slot,
+                               const int *kv_in_slots, const int *kv_out_slots, int logits_slot,
+                               int n_layers, int num_kv_heads, char *why, int why_len) {
+    if (!ctx || !kv_in_slots || !kv_out_slots) {
+        set_error("kllm_plan_match: NULL argument");
+        return -1;
+    }
+    PlanDesc pd;
+    pd.vocab = vocab_size;
+    pd.hidden = hidden_dim;
+    pd.head_dim = head_dim;
+    pd.embed_slot = token_embed_slot;
+    pd.cos_slot = rope_cos_slot;
+    pd.sin_slot = rope_sin_slot;
+    pd.kv_in = kv_in_slots;
+    pd.kv_out = kv_out_slots;
+    pd.logits_slot = logits_slot;
+    pd.n_layers = n_layers;
+    pd.n_kv = num_kv_heads;
+    std::string w;
+    bool ok = plan_match(ctx, pd, &w);
+    if (why && why_len > 0) {
+        snprintf(why, (size_t)why_len, "%s", ok ? "" : w.c_str());
+    }
+    return ok ? 1 : 0;
+}

@@ -1,30 +1,1019 @@
-// plan.cu -- fused decode plan (placeholder: the template is not matched
-// yet, so processor_infer runs the generic executor).
+// plan.cu -- fused decode plan for the compiler's LLaMA decode template.
+//
+// processor_infer drives one tape step per token (reference
+// _tape_runner.c:1602-1763).  When the tape is exactly the template the
+// kllm compiler emits (kllm_compile.c:1143-1385 per layer, driven by
+// :1427-1690), the plan replaces its ~60 instructions per layer by 7 fused
+// kernels over device-resident state:
+//
+//   resid_norm   h = embed[token] | h + sum_t part[t];  xn = rmsnorm(h) * w
+//   ttgemv       QKV partials                        (TMA, exact order)
+//   attention    RoPE(q,k), KV append in place, softmax(q.K^T * scale).V
+//   ttgemv       O partials
+//   resid_norm   h += O;  xn = rmsnorm(h) * w2
+//   ttgemv       gate_up partials
+//   ttgemv       down partials, x = silu(gate) * up fused into its load
+// then final resid_norm, the lm_head TT-GEMV and a multi-CTA logits +
+// first-maximum argmax that feeds the next step's embedding lookup.
+//
+// Arithmetic follows the tape op for op: every elementwise step is the
+// same float operation (no FMA contraction), SILU / EXP / RSQRT evaluate in
+// double, and the TT-GEMV keeps the reference's chunked order, so results
+// differ from the reference only where its summation order is not
+// reproducible at speed: the RMSNorm mean and softmax sums (a tree instead
+// of a serial loop) and the attention dot products (BLAS in the reference).
+//
+// Every kernel is launched with programmatic dependent launch: weight
+// streams and codebooks start before griddepcontrol.wait, so they overlap
+// the previous kernel.  Each step is captured once as a CUDA graph and
+// replayed; the step position and token live in device memory.
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <set>
+#include <vector>
+
 #include "plan.cuh"
+#include "sm100.cuh"
+#include "tt_kernels.cuh"
 
 namespace kllm {
 
-struct DecodePlan {};
+bool tt_gemv_tma_plain(cudaStream_t s, const CUtensorMap &map, const float *x, const float *cb,
+                       int n_codes, int K, int N, float *part, int *status, bool pdl);
+bool tt_gemv_tma_swiglu(cudaStream_t s, const CUtensorMap &map, const float *gu_part, int T_gu,
+                        int F, const float *cb, int n_codes, int K, int N, float *part,
+                        int *status, bool pdl);
+
+// ============================================================ matching ===
+
+struct LayerSlots {
+    int ln1 = -1, ln2 = -1, eps1 = -1, eps2 = -1;
+    int qkv = -1, o = -1, gu = -1, dn = -1;
+};
+
+struct TemplateInfo {
+    int H = 0, nh = 0, nkv = 0, hd = 0, F = 0, V = 0, L = 0, groups = 1;
+    int scale = -1, fln = -1, feps = -1, lm = -1;
+    std::vector<LayerSlots> layers;
+};
+
+namespace {
+
+struct Matcher {
+    const TapeCtx *ctx;
+    int pc = 0;
+    std::string why;
+    std::set<int> written;
+
+    const TapeInstr *next(int tag) {
+        if (!why.empty()) return nullptr;
+        if (pc >= ctx->n_instrs) {
+            why = "tape ends early";
+            return nullptr;
+        }
+        const TapeInstr *op = &ctx->tape[pc];
+        if (op->tag != tag) {
+            why = "instruction " + std::to_string(pc) + ": opcode " + std::to_string(op->tag) +
+                  ", template expects " + std::to_string(tag);
+            return nullptr;
+        }
+        if (op->out_slot < 0 || op->out_slot >= ctx->n_slots || written.count(op->out_slot)) {
+            why = "instruction " + std::to_string(pc) + ": output slot is not fresh";
+            return nullptr;
+        }
+        written.insert(op->out_slot);
+        pc++;
+        return op;
+    }
+    bool fail(const std::string &w) {
+        if (why.empty()) why = "instruction " + std::to_string(pc - 1) + ": " + w;
+        return false;
+    }
+    int unary(int tag, int in) {
+        const TapeInstr *op = next(tag);
+        if (!op) return -1;
+        if (op->in0 != in) return fail("unexpected operand"), -1;
+        return op->out_slot;
+    }
+    int binop(int tag, int a, int b) {   // b < 0: any slot, returned via *cap
+        const TapeInstr *op = next(tag);
+        if (!op) return -1;
+        if (op->in0 != a || (b >= 0 && op->in1 != b)) return fail("unexpected operands"), -1;
+        return op->out_slot;
+    }
+    const TapeInstr *binop_any(int tag, int a) {
+        const TapeInstr *op = next(tag);
+        if (op && op->in0 != a) return fail("unexpected operand"), nullptr;
+        return op;
+    }
+    int reduce(int tag, int in, int axis) {
+        const TapeInstr *op = next(tag);
+        if (!op) return -1;
+        if (op->in0 != in || op->axis != axis || op->keepdims != 1)
+            return fail("unexpected reduction"), -1;
+        return op->out_slot;
+    }
+    int slice(int in, std::initializer_list<int> starts, std::initializer_list<int> sizes) {
+        const TapeInstr *op = next(22);
+        if (!op) return -1;
+        int nd = (int)starts.size();
+        if (op->in0 != in || op->slice_out_ndim != nd) return fail("unexpected slice"), -1;
+        int d = 0;
+        for (int s : starts) {
+            if (op->starts[d] != s || op->steps[d] != 1) return fail("unexpected slice start"), -1;
+            d++;
+        }
+        d = 0;
+        for (int z : sizes) {
+            if (op->slice_out_shape[d] != z) return fail("unexpected slice size"), -1;
+            d++;
+        }
+        return op->out_slot;
+    }
+    int reshape(int in, std::initializer_list<int> shape) {
+        const TapeInstr *op = next(18);
+        if (!op) return -1;
+        if (op->in0 != in || op->out_ndim != (int)shape.size()) return fail("unexpected reshape"), -1;
+        int d = 0;
+        for (int z : shape)
+            if (op->out_shape[d++] != z) return fail("unexpected reshape shape"), -1;
+        return op->out_slot;
+    }
+    int transpose(int in, int a0, int a1, int a2) {
+        const TapeInstr *op = next(19);
+        if (!op) return -1;
+        if (op->in0 != in || op->axes[0] != a0 || op->axes[1] != a1 || op->axes[2] != a2)
+            return fail("unexpected transpose"), -1;
+        return op->out_slot;
+    }
+    int concat2(int a, int b, int axis) {
+        const TapeInstr *op = next(20);
+        if (!op) return -1;
+        if (op->concat_n_inputs != 2 || op->concat_inputs[0] != a || op->concat_inputs[1] != b ||
+            op->axis != axis)
+            return fail("unexpected concat"), -1;
+        return op->out_slot;
+    }
+    int repeat(int in, int reps, int axis) {
+        const TapeInstr *op = next(21);
+        if (!op) return -1;
+        if (op->in0 != in || op->repeats != reps || op->axis != axis)
+            return fail("unexpected repeat"), -1;
+        return op->out_slot;
+    }
+    int matmul(int a, int b) {
+        const TapeInstr *op = next(12);
+        if (!op) return -1;
+        if (op->in0 != a || op->in1 != b) return fail("unexpected matmul"), -1;
+        return op->out_slot;
+    }
+    // MATMUL_TT: returns out slot, weight slot via *w (must be a TT slot, K rows)
+    int matmul_tt(int a, int K, int *w) {
+        const TapeInstr *op = next(13);
+        if (!op) return -1;
+        if (op->in0 != a || op->in1 < 0 || op->in1 >= ctx->n_slots)
+            return fail("unexpected TT matmul"), -1;
+        const Slot &s = ctx->slots[op->in1];
+        if (!s.codebook || !s.w_indices || s.tt_K != K || s.n_codes <= 0)
+            return fail("TT weight slot missing or of the wrong shape"), -1;
+        *w = op->in1;
+        return op->out_slot;
+    }
+};
+
+bool const_slot(const TapeCtx *c, int s, int size) {
+    return s >= 0 && s < c->n_slots && c->slots[s].data && c->slots[s].size == size;
+}
+
+// RMSNorm of the template (kllm_compile.c:1143-1164): returns xn slot.
+int match_norm(Matcher &m, const TapeCtx *c, int h, int H, int *w_slot, int *eps_slot) {
+    int sq = m.binop(7, h, h);
+    int ms = m.reduce(16, sq, 1);
+    const TapeInstr *add = m.binop_any(5, ms);
+    if (!add) return -1;
+    *eps_slot = add->in1;
+    int rs = m.unary(2, add->out_slot);
+    int nm = m.binop(7, h, rs);
+    const TapeInstr *mw = m.binop_any(7, nm);
+    if (!mw) return -1;
+    *w_slot = mw->in1;
+    if (!const_slot(c, *eps_slot, 1) || !const_slot(c, *w_slot, H)) {
+        m.fail("norm constants missing");
+        return -1;
+    }
+    return mw->out_slot;
+}
+
+// RoPE of the template (kllm_compile.c:1172-1203).
+int match_rope(Matcher &m, int x, int cos_b, int sin_b, int heads, int hd) {
+    int half = hd / 2;
+    int x1 = m.slice(x, {0, 0, 0}, {heads, 1, half});
+    int x2 = m.slice(x, {0, 0, half}, {heads, 1, half});
+    int ng = m.unary(10, x2);
+    int rot = m.concat2(ng, x1, 2);
+    int xc = m.binop(7, x, cos_b);
+    int rs = m.binop(7, rot, sin_b);
+    return m.binop(5, xc, rs);
+}
+
+}  // namespace
+
+static bool match_template(const TapeCtx *ctx, const PlanDesc &d, TemplateInfo *ti,
+                           std::string *why) {
+    Matcher m{ctx};
+    TemplateInfo &t = *ti;
+    t.H = d.hidden;
+    t.hd = d.head_dim;
+    t.nkv = d.n_kv;
+    t.V = d.vocab;
+    t.L = d.n_layers;
+    if (t.H <= 0 || t.hd <= 0 || (t.hd & 1) || t.nkv <= 0 || t.V <= 0 || t.L <= 0) {
+        *why = "machine dimensions invalid";
+        return false;
+    }
+    int cos_b = -1, sin_b = -1;
+    {
+        const TapeInstr *c1 = m.next(23);
+        if (c1 && c1->in0 != d.cos_slot) m.fail("cos broadcast copy");
+        if (c1) cos_b = c1->out_slot;
+        const TapeInstr *c2 = m.next(23);
+        if (c2 && c2->in0 != d.sin_slot) m.fail("sin broadcast copy");
+        if (c2) sin_b = c2->out_slot;
+    }
+    int h = d.embed_slot;
+    for (int l = 0; l < t.L && m.why.empty(); l++) {
+        LayerSlots ls;
+        int xn = match_norm(m, ctx, h, t.H, &ls.ln1, &ls.eps1);
+        int qkv = m.matmul_tt(xn, t.H, &ls.qkv);
+        if (!m.why.empty()) break;
+        int nq = ctx->slots[ls.qkv].tt_N;
+        if (l == 0) {
+            int qd = nq - 2 * t.nkv * t.hd;
+            if (qd <= 0 || qd % t.hd) {
+                m.fail("QKV width does not split into heads");
+                break;
+            }
+            t.nh = qd / t.hd;
+            if (t.nh % t.nkv) {
+                m.fail("query heads not a multiple of KV heads");
+                break;
+            }
+            t.groups = t.nh / t.nkv;
+        }
+        int qd = t.nh * t.hd, kvd = t.nkv * t.hd;
+        if (nq != qd + 2 * kvd) {
+            m.fail("QKV width differs between layers");
+            break;
+        }
+        int q = m.slice(qkv, {0, 0}, {1, qd});
+        int k = m.slice(qkv, {0, qd}, {1, kvd});
+        int v = m.slice(qkv, {0, qd + kvd}, {1, kvd});
+        q = m.reshape(q, {1, t.nh, t.hd});
+        q = m.transpose(q, 1, 0, 2);
+        k = m.reshape(k, {1, t.nkv, t.hd});
+        k = m.transpose(k, 1, 0, 2);
+        v = m.reshape(v, {1, t.nkv, t.hd});
+        v = m.transpose(v, 1, 0, 2);
+        q = match_rope(m, q, cos_b, sin_b, t.nh, t.hd);
+        k = match_rope(m, k, cos_b, sin_b, t.nkv, t.hd);
+        int kf = m.concat2(d.kv_in[2 * l], k, 1);
+        int vf = m.concat2(d.kv_in[2 * l + 1], v, 1);
+        if (m.why.empty() && (kf != d.kv_out[2 * l] || vf != d.kv_out[2 * l + 1])) {
+            m.fail("KV outputs differ from the slot map");
+            break;
+        }
+        int ke = kf, ve = vf;
+        if (t.groups > 1) {
+            ke = m.repeat(kf, t.groups, 0);
+            ve = m.repeat(vf, t.groups, 0);
+        }
+        int kt = m.transpose(ke, 0, 2, 1);
+        int sc = m.matmul(q, kt);
+        const TapeInstr *scl = m.binop_any(7, sc);
+        if (!scl) break;
+        if (t.scale < 0) t.scale = scl->in1;
+        if (scl->in1 != t.scale || !const_slot(ctx, t.scale, 1)) {
+            m.fail("attention scale constant");
+            break;
+        }
+        int mx = m.reduce(15, scl->out_slot, 2);
+        int sub = m.binop(6, scl->out_slot, mx);
+        int ex = m.unary(1, sub);
+        int sm = m.reduce(14, ex, 2);
+        int aw = m.binop(8, ex, sm);
+        int cx = m.matmul(aw, ve);
+        cx = m.transpose(cx, 1, 0, 2);
+        cx = m.reshape(cx, {1, qd});
+        int at = m.matmul_tt(cx, qd, &ls.o);
+        int h1 = m.binop(5, h, at);
+        int xn2 = match_norm(m, ctx, h1, t.H, &ls.ln2, &ls.eps2);
+        int gu = m.matmul_tt(xn2, t.H, &ls.gu);
+        if (!m.why.empty()) break;
+        int F2 = ctx->slots[ls.gu].tt_N;
+        if (F2 % 2) {
+            m.fail("gate_up width is odd");
+            break;
+        }
+        if (l == 0) t.F = F2 / 2;
+        if (F2 != 2 * t.F) {
+            m.fail("gate_up width differs between layers");
+            break;
+        }
+        int g = m.slice(gu, {0, 0}, {1, t.F});
+        int u = m.slice(gu, {0, t.F}, {1, t.F});
+        int ga = m.unary(0, g);
+        int gd = m.binop(7, ga, u);
+        int dn = m.matmul_tt(gd, t.F, &ls.dn);
+        if (m.why.empty() && ctx->slots[ls.o].tt_N != t.H) m.fail("O projection width");
+        if (m.why.empty() && ctx->slots[ls.dn].tt_N != t.H) m.fail("down projection width");
+        h = m.binop(5, h1, dn);
+        t.layers.push_back(ls);
+    }
+    if (m.why.empty()) {
+        int xn = match_norm(m, ctx, h, t.H, &t.fln, &t.feps);
+        int lg = m.matmul_tt(xn, t.H, &t.lm);
+        if (m.why.empty() && (lg != d.logits_slot || ctx->slots[t.lm].tt_N != t.V))
+            m.fail("logits slot / vocabulary width");
+        if (m.why.empty() && m.pc != ctx->n_instrs) m.fail("tape continues after the logits");
+    }
+    if (!m.why.empty()) {
+        *why = m.why;
+        return false;
+    }
+    return true;
+}
+
+// ============================================================= kernels ===
+
+struct StepState {
+    int pos;          // position of the token fed this step
+    int prompt_len;
+    int n_gen;        // tokens generated so far
+    int counter;      // argmax CTA arrival counter
+};
+
+// h = embed row of this step's token (mode 0) or h + sum_t part[t]
+// (mode 1); xn = rmsnorm(h) * w  (kllm_compile.c:1143-1164: MUL, MEAN,
+// ADD eps, RSQRT in double, MUL, MUL).  One CTA; the sum of squares is a
+// fixed-shape tree, the rest is the tape's float arithmetic.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS)
+k_resid_norm(int mode, const float *__restrict__ embed, const StepState *st,
+             const int *__restrict__ prompt, const int *__restrict__ gen, int V,
+             const float *__restrict__ part, int T, float *__restrict__ h, int H,
+             const float *__restrict__ w, float eps, float inv_h, float *__restrict__ xn,
+             int *status) {
+    __shared__ float red[THREADS / 32];
+    __shared__ float s_rsq;
+    pdl_launch_dependents();
+    pdl_wait();
+    const float *src = nullptr;
+    if (mode == 0) {
+        int pos = st->pos, P = st->prompt_len;
+        int tok = pos < P ? prompt[pos] : gen[pos - P];
+        if (tok < 0 || tok >= V) {
+            if (threadIdx.x == 0) atomicOr(status, ST_BAD_TOKEN);
+            tok = 0;
+        }
+        src = embed + (size_t)tok * H;
+    }
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += THREADS) {
+        float v;
+        if (mode == 0) {
+            v = src[i];
+        } else {
+            float a = part[i];
+            for (int t = 1; t < T; t++) a = __fadd_rn(a, part[(size_t)t * H + i]);
+            v = __fadd_rn(h[i], a);
+        }
+        h[i] = v;
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < THREADS / 32 ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) {
+            float mean = __fmul_rn(v, inv_h);
+            float add = __fadd_rn(mean, eps);
+            s_rsq = (float)(1.0 / sqrt((double)add));
+        }
+    }
+    __syncthreads();
+    const float r = s_rsq;
+    for (int i = threadIdx.x; i < H; i += THREADS) xn[i] = __fmul_rn(__fmul_rn(h[i], r), w[i]);
+}
+
+// Attention for one query head (kllm_compile.c:1216-1343 after the QKV
+// projection): ordered chunk sums of the QKV partials, RoPE of q and k,
+// append of k/v at `pos` (by the first query head of each KV group),
+// scores q.k_j * scale over positions 0..pos, max-subtracted exp in double,
+// sum, divide, and the weighted sum of V.
+template <int HD, int THREADS>
+__global__ void __launch_bounds__(THREADS)
+k_attention(const StepState *st, const float *__restrict__ qkv_part, int T, int nq,
+            const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+            float *__restrict__ kc, float *__restrict__ vc, int max_pos, int groups, int nkv,
+            float scale, float *__restrict__ ctx_out) {
+    static_assert(HD % 32 == 0 && THREADS % HD == 0, "head_dim layout");
+    constexpr int DPL = HD / 32;          // dims per lane in the score loop
+    constexpr int NG = THREADS / HD;      // position groups in the V loop
+    extern __shared__ float sc[];         // [pos + 1] scores / weights
+    __shared__ float q[HD], k[HD], v[HD], red[THREADS / 32], part_ctx[NG][HD];
+    __shared__ float s_max, s_sum;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int hq = blockIdx.x, g = hq / groups, tid = threadIdx.x;
+    const int pos = st->pos;
+    if (pos >= max_pos) return;   // the host never launches past the KV capacity
+    const int qd = gridDim.x * HD, kvd = nkv * HD;
+    for (int i = tid; i < 3 * HD; i += THREADS) {
+        int which = i / HD, d = i % HD;
+        int col = which == 0 ? hq * HD + d : (which == 1 ? qd + g * HD + d : qd + kvd + g * HD + d);
+        float a = qkv_part[col];
+        for (int t = 1; t < T; t++) a = __fadd_rn(a, qkv_part[(size_t)t * nq + col]);
+        (which == 0 ? q : which == 1 ? k : v)[d] = a;
+    }
+    __syncthreads();
+    // RoPE: x*cos + rotate_half(x)*sin, rotate_half = concat(-x2, x1)
+    float qr = 0.f, kr = 0.f;
+    if (tid < HD) {
+        const float c = rope_cos[(size_t)pos * HD + tid], s = rope_sin[(size_t)pos * HD + tid];
+        const int half = HD / 2;
+        float rq = tid < half ? -q[tid + half] : q[tid - half];
+        float rk = tid < half ? -k[tid + half] : k[tid - half];
+        qr = __fadd_rn(__fmul_rn(q[tid], c), __fmul_rn(rq, s));
+        kr = __fadd_rn(__fmul_rn(k[tid], c), __fmul_rn(rk, s));
+    }
+    __syncthreads();
+    if (tid < HD) {
+        q[tid] = qr;
+        k[tid] = kr;
+        if (hq % groups == 0) {
+            size_t o = ((size_t)g * max_pos + pos) * HD + tid;
+            kc[o] = kr;
+            vc[o] = v[tid];
+        }
+    }
+    __syncthreads();
+    // scores: one warp per position, DPL dims per lane, xor-tree sum
+    const int warp = tid >> 5, lane = tid & 31;
+    float qv[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; i++) qv[i] = q[lane + 32 * i];
+    for (int j = warp; j <= pos; j += THREADS / 32) {
+        const float *kj = j == pos ? k : kc + ((size_t)g * max_pos + j) * HD;
+        float dot = __fmul_rn(qv[0], kj[lane]);
+#pragma unroll
+        for (int i = 1; i < DPL; i++) dot = __fadd_rn(dot, __fmul_rn(qv[i], kj[lane + 32 * i]));
+        for (int o = 16; o; o >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
+        if (lane == 0) sc[j] = __fmul_rn(dot, scale);
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int j = tid; j <= pos; j += THREADS) m = fmaxf(m, sc[j]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int i = 1; i < THREADS / 32; i++) mm = fmaxf(mm, red[i]);
+        s_max = mm;
+    }
+    __syncthreads();
+    const float mx = s_max;
+    float sum = 0.f;
+    for (int j = tid; j <= pos; j += THREADS) {
+        float e = (float)exp((double)__fsub_rn(sc[j], mx));
+        sc[j] = e;
+        sum = __fadd_rn(sum, e);
+    }
+    for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        float ss = red[0];
+        for (int i = 1; i < THREADS / 32; i++) ss = __fadd_rn(ss, red[i]);
+        s_sum = ss;
+    }
+    __syncthreads();
+    const float tot = s_sum;
+    for (int j = tid; j <= pos; j += THREADS) sc[j] = __fdiv_rn(sc[j], tot);
+    __syncthreads();
+    // ctx[d] = sum_j p_j * v_j[d]: NG position groups per dim
+    const int d = tid % HD, grp = tid / HD;
+    float acc = 0.f;
+    for (int j = grp; j <= pos; j += NG) {
+        float vj = j == pos ? v[d] : vc[((size_t)g * max_pos + j) * HD + d];
+        acc = __fadd_rn(acc, __fmul_rn(sc[j], vj));
+    }
+    part_ctx[grp][d] = acc;
+    __syncthreads();
+    if (tid < HD) {
+        float a = part_ctx[0][tid];
+        for (int i = 1; i < NG; i++) a = __fadd_rn(a, part_ctx[i][tid]);
+        ctx_out[hq * HD + tid] = a;
+    }
+}
+
+// logits[v] = ordered chunk sum of the lm_head partials, then the
+// first-maximum argmax across CTAs (_tape_runner.c:1717-1727); the last CTA
+// to finish publishes the token and advances the step.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS)
+k_logits_argmax(StepState *st, const float *__restrict__ part, int T, int V,
+                float *__restrict__ logits, float *__restrict__ hist, int hist_rows,
+                float *__restrict__ cand_v, int *__restrict__ cand_i, int *__restrict__ gen,
+                volatile int *gen_host, int max_gen) {
+    __shared__ float rv[THREADS / 32];
+    __shared__ int ri[THREADS / 32];
+    __shared__ bool last;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int pos = st->pos;
+    const int per = (V + gridDim.x - 1) / gridDim.x;
+    const int v0 = blockIdx.x * per, v1 = min(V, v0 + per);
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = v0 + threadIdx.x; i < v1; i += THREADS) {
+        float a = part[i];
+        for (int t = 1; t < T; t++) a = __fadd_rn(a, part[(size_t)t * V + i]);
+        logits[i] = a;
+        if (hist && pos < hist_rows) hist[(size_t)pos * V + i] = a;
+        if (a > bv || (a == bv && i < bi) || bi == 0x7fffffff) {
+            bv = a;
+            bi = i;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        rv[threadIdx.x >> 5] = bv;
+        ri[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < THREADS / 32; w++)
+            if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) {
+                bv = rv[w];
+                bi = ri[w];
+            }
+        cand_v[blockIdx.x] = bv;
+        cand_i[blockIdx.x] = bi;
+        __threadfence();
+        last = atomicAdd(&st->counter, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float best = cand_v[0];
+    int bidx = cand_i[0];
+    for (int b = 1; b < (int)gridDim.x; b++) {
+        float cv = ((volatile float *)cand_v)[b];
+        int ci = ((volatile int *)cand_i)[b];
+        if (cv > best || (cv == best && ci < bidx)) {
+            best = cv;
+            bidx = ci;
+        }
+    }
+    if (bidx < 0 || bidx >= V) bidx = 0;
+    const int P = st->prompt_len;
+    if (pos >= P - 1) {
+        int gi = pos - (P - 1);
+        if (gi < max_gen) {
+            gen[gi] = bidx;
+            gen_host[gi] = bidx;
+            __threadfence_system();
+        }
+        st->n_gen = gi + 1;
+    }
+    st->counter = 0;
+    st->pos = pos + 1;
+}
+
+// ================================================================ plan ===
+
+struct DecodePlan {
+    TemplateInfo ti;
+    int max_pos = 0;
+    int T_h = 0, T_qd = 0, T_f = 0;   // chunk counts by K
+    const float *src_embed = nullptr;
+    const float *src_cos = nullptr, *src_sin = nullptr;
+    // device state
+    float *embed = nullptr, *rcos = nullptr, *rsin = nullptr;
+    float *h = nullptr, *xn = nullptr, *ctx = nullptr, *logits = nullptr;
+    float *p_qkv = nullptr, *p_o = nullptr, *p_gu = nullptr, *p_dn = nullptr, *p_lm = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float *cand_v = nullptr;
+    int *cand_i = nullptr;
+    StepState *st = nullptr;
+    int *prompt = nullptr, *gen = nullptr, *status = nullptr;
+    int *gen_host = nullptr;   // mapped pinned
+    int *gen_host_dev = nullptr;
+    float *hist = nullptr;
+    int hist_rows = 0;
+    std::vector<float> norm_w;   // not used on device; kept for checks
+    std::vector<float *> dev_norm;
+    std::vector<float> eps;
+    float scale = 0.f, f_eps = 0.f;
+    std::vector<CUtensorMap> maps;   // per layer: qkv, o, gu, dn ; then lm
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    float *graph_hist = nullptr;   // history buffer baked into the graph
+    int graph_hist_rows = 0;
+    int logits_slot = -1;
+    int argmax_ctas = 148;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
+    std::vector<cudaEvent_t> step_ev;
+};
+
+static void free_plan(DecodePlan *p) {
+    if (!p) return;
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->xn, p->ctx, p->logits, p->p_qkv,
+                    p->p_o, p->p_gu, p->p_dn, p->p_lm, p->kc, p->vc, p->cand_v, p->cand_i,
+                    p->st, p->prompt, p->gen, p->status, p->hist};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    for (float *b : p->dev_norm)
+        if (b) cudaFree(b);
+    if (p->gen_host) cudaFreeHost(p->gen_host);
+    for (cudaEvent_t e : {p->ev0, p->ev1, p->ev2})
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : p->step_ev) cudaEventDestroy(e);
+    delete p;
+}
+
+void plan_destroy(CtxImpl *c) {
+    if (c->plan) {
+        cudaSetDevice(c->device);
+        if (c->stream) cudaStreamSynchronize(c->stream);
+        free_plan(c->plan);
+    }
+    c->plan = nullptr;
+}
+
+template <class T>
+static bool dalloc(T **p, size_t n) {
+    return KLLM_CUDA(cudaMalloc((void **)p, std::max<size_t>(n, 1) * sizeof(T)));
+}
+
+bool plan_match(const TapeCtx *ctx, const PlanDesc &d, std::string *why) {
+    TemplateInfo ti;
+    return match_template(ctx, d, &ti, why);
+}
 
 bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) {
-    (void)c;
-    (void)d;
-    (void)max_pos;
-    *why = "fused plan not built";
-    return false;
+    TapeCtx *ctx = &c->base;
+    DecodePlan *old = c->plan;
+    if (old && old->max_pos >= max_pos && old->src_embed == d.embed &&
+        old->src_cos == d.rope_cos && old->src_sin == d.rope_sin && old->ti.H == d.hidden &&
+        old->ti.V == d.vocab) {
+        return true;   // reuse (weights are re-checked by upload_tt below)
+    }
+    TemplateInfo ti;
+    if (!match_template(ctx, d, &ti, why)) return false;
+    if (ti.hd != 32 && ti.hd != 64 && ti.hd != 128) {
+        *why = "head_dim " + std::to_string(ti.hd) + " (fused attention covers 32, 64, 128)";
+        return false;
+    }
+    if ((size_t)max_pos * 4 > 160 * 1024) {
+        *why = "context longer than the fused attention's score buffer";
+        return false;
+    }
+    static bool att_attr[64] = {};
+    if (!att_attr[c->device & 63]) {
+        for (auto f : {k_attention<32, 256>, k_attention<64, 256>, k_attention<128, 256>})
+            if (!KLLM_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                160 * 1024)))
+                return false;
+        att_attr[c->device & 63] = true;
+    }
+    plan_destroy(c);
+    DecodePlan *p = new DecodePlan();
+    p->ti = ti;
+    p->max_pos = max_pos;
+    p->src_embed = d.embed;
+    p->src_cos = d.rope_cos;
+    p->src_sin = d.rope_sin;
+    p->logits_slot = d.logits_slot;
+    const int H = ti.H, V = ti.V, L = ti.L, hd = ti.hd, nkv = ti.nkv;
+    const int qd = ti.nh * hd, nq = qd + 2 * nkv * hd, F = ti.F;
+    p->T_h = tt_chunks(H);
+    p->T_qd = tt_chunks(qd);
+    p->T_f = tt_chunks(F);
+    auto fail = [&]() {
+        free_plan(p);
+        return false;
+    };
+    // weights: the context's device copies of the TT slots
+    std::vector<int> tts;
+    for (auto &ls : ti.layers) tts.insert(tts.end(), {ls.qkv, ls.o, ls.gu, ls.dn});
+    tts.push_back(ti.lm);
+    for (int s : tts) {
+        if (!upload_tt(c, s)) return fail();
+        const Slot &sl = ctx->slots[s];
+        if (!tt_tma_ok(c->ds[s].d_idx, sl.tt_K, sl.tt_N, sl.n_codes)) {
+            *why = "a weight matrix does not meet the TMA alignment rules";
+            free_plan(p);
+            return false;
+        }
+    }
+    p->maps.resize(tts.size());
+    for (size_t i = 0; i < tts.size(); i++) {
+        const Slot &sl = ctx->slots[tts[i]];
+        if (!make_idx_tmap(&p->maps[i], c->ds[tts[i]].d_idx, sl.tt_K, sl.tt_N, 128, 32))
+            return fail();
+    }
+    // norm weights and constants
+    for (auto &ls : ti.layers) {
+        for (int s : {ls.ln1, ls.ln2}) {
+            float *dw = nullptr;
+            if (!dalloc(&dw, H)) return fail();
+            p->dev_norm.push_back(dw);
+            if (!KLLM_CUDA(cudaMemcpy(dw, ctx->slots[s].data, (size_t)H * 4,
+                                      cudaMemcpyHostToDevice)))
+                return fail();
+        }
+        p->eps.push_back(ctx->slots[ls.eps1].data[0]);
+        p->eps.push_back(ctx->slots[ls.eps2].data[0]);
+    }
+    {
+        float *dw = nullptr;
+        if (!dalloc(&dw, H)) return fail();
+        p->dev_norm.push_back(dw);
+        if (!KLLM_CUDA(cudaMemcpy(dw, ctx->slots[ti.fln].data, (size_t)H * 4,
+                                  cudaMemcpyHostToDevice)))
+            return fail();
+        p->f_eps = ctx->slots[ti.feps].data[0];
+    }
+    p->scale = ctx->slots[ti.scale].data[0];
+    // tables
+    if (!dalloc(&p->embed, (size_t)V * H) ||
+        !KLLM_CUDA(cudaMemcpy(p->embed, d.embed, (size_t)V * H * 4, cudaMemcpyHostToDevice)) ||
+        !dalloc(&p->rcos, (size_t)max_pos * hd) || !dalloc(&p->rsin, (size_t)max_pos * hd) ||
+        !KLLM_CUDA(cudaMemcpy(p->rcos, d.rope_cos, (size_t)max_pos * hd * 4,
+                              cudaMemcpyHostToDevice)) ||
+        !KLLM_CUDA(cudaMemcpy(p->rsin, d.rope_sin, (size_t)max_pos * hd * 4,
+                              cudaMemcpyHostToDevice)))
+        return fail();
+    // activations, partials, KV cache, step state
+    size_t kv = (size_t)L * nkv * max_pos * hd;
+    if (!dalloc(&p->h, H) || !dalloc(&p->xn, std::max(H, F)) || !dalloc(&p->ctx, qd) ||
+        !dalloc(&p->logits, V) || !dalloc(&p->p_qkv, (size_t)p->T_h * nq) ||
+        !dalloc(&p->p_o, (size_t)p->T_qd * H) || !dalloc(&p->p_gu, (size_t)p->T_h * 2 * F) ||
+        !dalloc(&p->p_dn, (size_t)p->T_f * H) || !dalloc(&p->p_lm, (size_t)p->T_h * V) ||
+        !dalloc(&p->kc, kv) || !dalloc(&p->vc, kv) || !dalloc(&p->cand_v, 1024) ||
+        !dalloc(&p->cand_i, 1024) || !dalloc(&p->st, 1) || !dalloc(&p->prompt, max_pos) ||
+        !dalloc(&p->gen, max_pos) || !dalloc(&p->status, 1))
+        return fail();
+    if (!KLLM_CUDA(cudaMemset(p->kc, 0, kv * 4)) || !KLLM_CUDA(cudaMemset(p->vc, 0, kv * 4)) ||
+        !KLLM_CUDA(cudaMemset(p->st, 0, sizeof(StepState))))
+        return fail();
+    if (!KLLM_CUDA(cudaHostAlloc((void **)&p->gen_host, (size_t)max_pos * 4,
+                                 cudaHostAllocMapped)) ||
+        !KLLM_CUDA(cudaHostGetDevicePointer((void **)&p->gen_host_dev, p->gen_host, 0)))
+        return fail();
+    if (!KLLM_CUDA(cudaEventCreate(&p->ev0)) || !KLLM_CUDA(cudaEventCreate(&p->ev1)) ||
+        !KLLM_CUDA(cudaEventCreate(&p->ev2)))
+        return fail();
+    int argc = 148;
+    cudaDeviceGetAttribute(&argc, cudaDevAttrMultiProcessorCount, c->device);
+    p->argmax_ctas = std::min(std::max(1, (V + 255) / 256), std::min(argc, 1024));
+    c->plan = p;
+    return true;
+}
+
+template <class Kern, class... Args>
+static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t smem,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    g_launches++;
+    return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
+}
+
+// All kernels of one tape step, in stream order.
+static bool record_step(CtxImpl *c, DecodePlan *p) {
+    cudaStream_t s = c->stream;
+    const TemplateInfo &t = p->ti;
+    const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, nq = qd + 2 * nkv * hd;
+    const int F = t.F, V = t.V;
+    const float inv_h = 1.0f / (float)H;
+    const TapeCtx *ctx = &c->base;
+    constexpr int NT = 1024;
+    for (int l = 0; l < t.L; l++) {
+        const LayerSlots &ls = t.layers[l];
+        const DevSlot &wq = c->ds[ls.qkv], &wo = c->ds[ls.o], &wg = c->ds[ls.gu],
+                      &wd = c->ds[ls.dn];
+        // residual (from the previous layer's down projection) + norm 1
+        if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, l == 0 ? 0 : 1,
+                        (const float *)p->embed, (const StepState *)p->st, (const int *)p->prompt,
+                        (const int *)p->gen, V, (const float *)p->p_dn, p->T_f, p->h, H,
+                        (const float *)p->dev_norm[2 * l], p->eps[2 * l], inv_h, p->xn,
+                        p->status))
+            return false;
+        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 0], p->xn, wq.d_cb, ctx->slots[ls.qkv].n_codes,
+                               H, nq, p->p_qkv, p->status, true))
+            return false;
+        size_t smem_att = (size_t)p->max_pos * 4;
+        auto att = hd == 32 ? k_attention<32, 256> : hd == 64 ? k_attention<64, 256>
+                                                              : k_attention<128, 256>;
+        if (!launch_pdl(s, att, dim3(t.nh), dim3(256), smem_att, (const StepState *)p->st,
+                        (const float *)p->p_qkv, p->T_h, nq, (const float *)p->rcos,
+                        (const float *)p->rsin, p->kc + (size_t)l * nkv * p->max_pos * hd,
+                        p->vc + (size_t)l * nkv * p->max_pos * hd, p->max_pos, t.groups, nkv,
+                        p->scale, p->ctx))
+            return false;
+        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 1], p->ctx, wo.d_cb, ctx->slots[ls.o].n_codes,
+                               qd, H, p->p_o, p->status, true))
+            return false;
+        if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, 1, (const float *)p->embed,
+                        (const StepState *)p->st, (const int *)p->prompt, (const int *)p->gen, V,
+                        (const float *)p->p_o, p->T_qd, p->h, H,
+                        (const float *)p->dev_norm[2 * l + 1], p->eps[2 * l + 1], inv_h, p->xn,
+                        p->status))
+            return false;
+        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 2], p->xn, wg.d_cb, ctx->slots[ls.gu].n_codes,
+                               H, 2 * F, p->p_gu, p->status, true))
+            return false;
+        if (!tt_gemv_tma_swiglu(s, p->maps[4 * l + 3], p->p_gu, p->T_h, F, wd.d_cb,
+                                ctx->slots[ls.dn].n_codes, F, H, p->p_dn, p->status, true))
+            return false;
+    }
+    if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, 1, (const float *)p->embed,
+                    (const StepState *)p->st, (const int *)p->prompt, (const int *)p->gen, V,
+                    (const float *)p->p_dn, p->T_f, p->h, H, (const float *)p->dev_norm.back(),
+                    p->f_eps, inv_h, p->xn, p->status))
+        return false;
+    const DevSlot &wl = c->ds[t.lm];
+    if (!tt_gemv_tma_plain(s, p->maps.back(), p->xn, wl.d_cb, ctx->slots[t.lm].n_codes, H, V,
+                           p->p_lm, p->status, true))
+        return false;
+    if (!launch_pdl(s, k_logits_argmax<256>, dim3(p->argmax_ctas), dim3(256), 0, p->st,
+                    (const float *)p->p_lm, p->T_h, V, p->logits, p->hist, p->hist_rows,
+                    p->cand_v, p->cand_i, p->gen, (volatile int *)p->gen_host_dev, p->max_pos))
+        return false;
+    return true;
+}
+
+static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
+    if (p->exec && p->graph_hist == p->hist && p->graph_hist_rows == p->hist_rows) return true;
+    if (p->exec) cudaGraphExecDestroy(p->exec);
+    if (p->graph) cudaGraphDestroy(p->graph);
+    p->exec = nullptr;
+    p->graph = nullptr;
+    if (!KLLM_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal)))
+        return false;
+    bool ok = record_step(c, p);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (!ok || !KLLM_CUDA(e)) {
+        if (g) cudaGraphDestroy(g);
+        return false;
+    }
+    p->graph = g;
+    if (!KLLM_CUDA(cudaGraphInstantiate(&p->exec, g, 0))) return false;
+    p->graph_hist = p->hist;
+    p->graph_hist_rows = p->hist_rows;
+    return true;
 }
 
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,
                 int eos, const std::function<bool(int, int)> &emit, int *generated) {
-    (void)c; (void)prompt; (void)prompt_len; (void)max_new; (void)max_pos; (void)eos;
-    (void)emit; (void)generated;
-    set_error("fused plan not built");
-    return false;
-}
-
-void plan_destroy(CtxImpl *c) {
-    delete c->plan;
-    c->plan = nullptr;
+    DecodePlan *p = c->plan;
+    *generated = 0;
+    if (!p || max_pos > p->max_pos) {
+        set_error("decode plan not prepared");
+        return false;
+    }
+    const int V = p->ti.V;
+    for (int i = 0; i < prompt_len; i++)
+        if (prompt[i] < 0 || prompt[i] >= V) {
+            set_error("prompt token %d (%d) outside the vocabulary of %d", i, prompt[i], V);
+            return false;
+        }
+    cudaStream_t s = c->stream;
+    // logits history for callers that asked for every step's logits
+    int want_rows = c->opts.logits_out ? std::min(c->opts.logits_rows, max_pos) : 0;
+    if (want_rows > 0 && (!p->hist || p->hist_rows < want_rows)) {
+        if (p->hist) cudaFree(p->hist);
+        p->hist = nullptr;
+        if (!dalloc(&p->hist, (size_t)want_rows * V)) return false;
+        p->hist_rows = want_rows;
+    } else if (want_rows == 0 && p->hist) {
+        cudaFree(p->hist);
+        p->hist = nullptr;
+        p->hist_rows = 0;
+    }
+    StepState st0 = {0, prompt_len, 0, 0};
+    if (!KLLM_CUDA(cudaMemcpyAsync(p->prompt, prompt, (size_t)prompt_len * 4,
+                                   cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemcpyAsync(p->st, &st0, sizeof st0, cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemsetAsync(p->status, 0, 4, s)) ||
+        !KLLM_CUDA(cudaStreamSynchronize(s)))
+        return false;
+    for (int i = 0; i < max_pos; i++) p->gen_host[i] = -1;
+    bool graphs = c->opts.use_graphs != 0;
+    if (graphs && !ensure_graph(c, p)) return false;
+    // positions are capped at max_pos (the bytes driver's max_seq_tokens,
+    // _tape_runner.c:1537): at most max_pos - prompt_len tokens
+    const int max_gen = std::max(0, std::min(max_new, max_pos - prompt_len));
+    const int total = prompt_len + max_gen;
+    if ((int)p->step_ev.size() < total) {
+        size_t old = p->step_ev.size();
+        p->step_ev.resize(total);
+        for (size_t i = old; i < p->step_ev.size(); i++)
+            if (!KLLM_CUDA(cudaEventCreateWithFlags(&p->step_ev[i], cudaEventDisableTiming)))
+                return false;
+    }
+    auto launch_step = [&](int i) -> bool {
+        bool ok = graphs ? KLLM_CUDA(cudaGraphLaunch(p->exec, s)) : record_step(c, p);
+        return ok && KLLM_CUDA(cudaEventRecord(p->step_ev[i], s));
+    };
+    if (!KLLM_CUDA(cudaEventRecord(p->ev0, s))) return false;
+    int launched = 0;
+    for (; launched < prompt_len; launched++)
+        if (!launch_step(launched)) return false;
+    if (!KLLM_CUDA(cudaEventRecord(p->ev1, s))) return false;
+    // decode: keep the device ahead of the host by up to `window` steps
+    const int window = 64;
+    int gen = 0;
+    bool stop = false;
+    while (!stop && gen < max_gen) {
+        while (launched < total && launched - (prompt_len - 1 + gen) <= window)
+            if (!launch_step(launched++)) return false;
+        // token `gen` is produced by step prompt_len - 1 + gen
+        if (!KLLM_CUDA(cudaEventSynchronize(p->step_ev[prompt_len - 1 + gen]))) return false;
+        int tok = ((volatile int *)p->gen_host)[gen];
+        if (tok == eos) break;
+        gen++;
+        if (!emit(tok, gen - 1)) stop = true;
+    }
+    // the reference also feeds the last generated token (one more step)
+    if (!stop && gen == max_gen) {
+        while (launched < total)
+            if (!launch_step(launched++)) return false;
+    }
+    if (!KLLM_CUDA(cudaEventRecord(p->ev2, s)) || !KLLM_CUDA(cudaStreamSynchronize(s)))
+        return false;
+    int status = 0;
+    if (!KLLM_CUDA(cudaMemcpy(&status, p->status, 4, cudaMemcpyDeviceToHost))) return false;
+    if (status) {
+        set_error("decode kernels reported status 0x%x (%s)", status,
+                  (status & ST_WAIT_TIMEOUT) ? "a wait timed out" : "a token was out of range");
+        return false;
+    }
+    float pre = 0.f, dec = 0.f;
+    cudaEventElapsedTime(&pre, p->ev0, p->ev1);
+    cudaEventElapsedTime(&dec, p->ev1, p->ev2);
+    c->stats.prefill_ms = pre;
+    c->stats.decode_ms = dec;
+    c->stats.steps = prompt_len + gen;
+    *generated = gen;
+    if (want_rows > 0) {
+        int rows = std::min(want_rows, prompt_len + gen);
+        if (!KLLM_CUDA(cudaMemcpy(c->opts.logits_out, p->hist, (size_t)rows * V * 4,
+                                  cudaMemcpyDeviceToHost)))
+            return false;
+    }
+    // leave the last step's logits in the logits slot, as the tape would
+    // (only when no step ran past it)
+    int ls = p->logits_slot;
+    if (ls >= 0 && launched == prompt_len + gen) {
+        Slot &sl = c->base.slots[ls];
+        if (ensure_device(c, ls, (size_t)V) &&
+            KLLM_CUDA(cudaMemcpyAsync(c->ds[ls].d, p->logits, (size_t)V * 4,
+                                      cudaMemcpyDeviceToDevice, s))) {
+            sl.ndim = 2;
+            sl.shape[0] = 1;
+            sl.shape[1] = V;
+            if (sl.size < V) sl.size = V;
+            c->ds[ls].dev_newer = true;
+            c->ds[ls].host_dirty = false;
+        }
+    }
+    return KLLM_CUDA(cudaStreamSynchronize(s));
 }
 
 }  // namespace kllm

@@ -19,6 +19,9 @@ struct PlanDesc {
     int logits_slot = -1, n_layers = 0, n_kv = 0;
 };
 
+// Whether the tape is the compiler's template (no device work).
+bool plan_match(const TapeCtx *ctx, const PlanDesc &d, std::string *why);
+
 // Match the tape against the template and stage the plan's device state
 // (weights, KV cache for max_pos positions, graphs).  Returns false with a
 // reason when the tape is not the template; no error is recorded then.

@@ -10,12 +10,20 @@
 //   * the chunk sums are added in chunk order (_tape_runner.c:646-662).
 // Every (column, chunk) chain is an independent serial sum, so the device
 // parallelises over columns x chunks and writes T partial rows; a second
-// pass adds them in order.  __fmul_rn/__fadd_rn keep the compiler from
-// contracting the product and the add into one FMA.
+// pass (or the consuming kernel) adds them in order.  __fmul_rn/__fadd_rn
+// keep the compiler from contracting the product and the add into one FMA.
+//
+// Two kernels: the TMA-staged one (tt_kernels.cuh) for 16-byte aligned
+// matrices with N % 8 == 0 and codebooks up to 16384 entries, and a simple
+// one (indices straight from HBM, codebook through the read-only cache) for
+// everything else.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
+#include "tt_kernels.cuh"
 
 namespace kllm {
 
@@ -32,6 +40,36 @@ void tt_chunk_range(int K, int T, int t, int *k0, int *len) {
     int base = K / T, rem = K % T;
     *k0 = t * base + std::min(t, rem);
     *len = base + (t < rem ? 1 : 0);
+}
+
+bool make_idx_tmap(CUtensorMap *map, const uint16_t *idx, int K, int N, int box_cols,
+                   int box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    });
+    if (!encode) {
+        set_error("cuTensorMapEncodeTiled is not available from the driver");
+        return false;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+    cuuint64_t strides[1] = {(cuuint64_t)N * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)idx, dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for a %dx%d index matrix", (int)r, K, N);
+        return false;
+    }
+    return true;
 }
 
 // ------------------------------------------------------ simple kernel ----
@@ -60,10 +98,72 @@ __global__ void k_tt_gemv_simple(const float *__restrict__ x, int rows,
     }
 }
 
+// Decode-shape configuration of the TMA kernel: 2 consumer warps x 2
+// columns per lane = 128 columns per CTA, 32-row boxes (8 KB), up to 8
+// stages in flight.
+constexpr int kNCW = 2, kCPL = 2, kBR = 32, kMaxStages = 8;
+using Geo = TTGeom<kNCW, kCPL, kBR>;
+
+int tt_tma_stages(int n_codes, int len) {
+    int nbox = (len + kBR - 1) / kBR;
+    int ns = std::min(kMaxStages, std::max(nbox, 1));
+    while (ns > 2 && tt_smem_bytes<kNCW, kCPL, kBR>(n_codes, len, ns) > 110 * 1024) ns--;
+    return ns;
+}
+
+template <class XS>
+static bool launch_tma(cudaStream_t s, const CUtensorMap &map, const float *cb, int n_codes,
+                       const XS &xs, int K, int N, float *part, int *status, bool pdl) {
+    int T = tt_chunks(K);
+    int maxlen = (K + T - 1) / T;
+    int ns = tt_tma_stages(n_codes, maxlen);
+    size_t smem = tt_smem_bytes<kNCW, kCPL, kBR>(n_codes, maxlen, ns);
+    auto kern = k_ttgemv_tma<kNCW, kCPL, kBR, XS>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (!KLLM_CUDA(cudaGetDevice(&dev))) return false;
+    if (!attr_set[dev & 63]) {
+        if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024)))
+            return false;
+        attr_set[dev & 63] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((N + Geo::BN - 1) / Geo::BN, T);
+    cfg.blockDim = dim3(Geo::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    g_launches++;
+    return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, map, cb, n_codes, xs, K, N, T, ns, part,
+                                        status));
+}
+
+bool tt_gemv_tma_plain(cudaStream_t s, const CUtensorMap &map, const float *x, const float *cb,
+                       int n_codes, int K, int N, float *part, int *status, bool pdl) {
+    return launch_tma(s, map, cb, n_codes, XPlain{x}, K, N, part, status, pdl);
+}
+
+// x = silu(gate) * up from the gate_up projection's T_gu partial rows.
+bool tt_gemv_tma_swiglu(cudaStream_t s, const CUtensorMap &map, const float *gu_part, int T_gu,
+                        int F, const float *cb, int n_codes, int K, int N, float *part,
+                        int *status, bool pdl) {
+    XSwiGLU xs{gu_part, T_gu, F, 2LL * F};
+    return launch_tma(s, map, cb, n_codes, xs, K, N, part, status, pdl);
+}
+
 bool tt_gemv_partials(cudaStream_t s, const float *x, int rows, const float *cb, int n_codes,
                       const uint16_t *idx, int K, int N, float *part) {
-    (void)n_codes;
     int T = tt_chunks(K);
+    if (rows == 1 && tt_tma_ok(idx, K, N, n_codes)) {
+        CUtensorMap map;
+        if (!make_idx_tmap(&map, idx, K, N, Geo::BN, kBR)) return false;
+        return tt_gemv_tma_plain(s, map, x, cb, n_codes, K, N, part, nullptr, false);
+    }
     dim3 grid((N + 127) / 128, T);
     k_tt_gemv_simple<<<grid, 128, 0, s>>>(x, rows, cb, idx, K, N, T, part);
     g_launches++;
@@ -145,6 +245,18 @@ extern "C" int kllm_tt_gemv_host(const float *x, int rows, const float *codebook
     }
     if (rows == 0 || N == 0) return 0;
     size_t nx = (size_t)rows * K, ni = (size_t)K * N, ny = (size_t)rows * N;
+    if (!idx || !codebook || !x || !y) {
+        set_error("kllm_tt_gemv_host: NULL argument");
+        return -1;
+    }
+    if (n_codes < 65536) {
+        for (size_t i = 0; i < ni; i++)
+            if (idx[i] >= n_codes) {
+                set_error("kllm_tt_gemv_host: index %u at %zu outside the codebook of %d",
+                          (unsigned)idx[i], i, n_codes);
+                return -1;
+            }
+    }
     size_t ncb = ((size_t)n_codes + 3) & ~(size_t)3;
     float *dx = nullptr, *dcb = nullptr, *dy = nullptr;
     uint16_t *di = nullptr;

@@ -297,24 +297,5 @@ class OracleChip:
             self.ctx = None
 
 
-def gaussian_rank_indices(rng, K, N, n_codes, sigma=0.02, codebook=None):
-    """uint16 indices whose code frequencies follow the Gaussian rank that
-    bf16-rounding N(0, sigma) produces: draw w ~ N(0, sigma) and take the
-    nearest codebook entry (the codebook is sorted)."""
-    w = rng.standard_normal((K, N), dtype=np.float32) * np.float32(sigma)
-    pos = np.searchsorted(codebook, w)
-    pos = np.clip(pos, 1, n_codes - 1)
-    left = codebook[pos - 1]
-    right = codebook[pos]
-    pick = np.where(np.abs(w - left) <= np.abs(right - w), pos - 1, pos)
-    return pick.astype(np.uint16)
-
-
-def tt_case(seed, K, N, n_codes, rows=1):
-    """A config-1 style TT-GEMV case: sorted seeded N(0,0.02) codebook,
-    Gaussian-rank indices, x ~ N(0,1)."""
-    rng = np.random.default_rng(seed)
-    cb = np.sort(rng.standard_normal(n_codes).astype(np.float32) * np.float32(0.02))
-    idx = gaussian_rank_indices(rng, K, N, n_codes, codebook=cb)
-    x = rng.standard_normal((rows, K), dtype=np.float32)
-    return x, cb, idx
+gaussian_rank_indices = chipgen.gaussian_rank_indices
+tt_case = chipgen.tt_case

@@ -95,3 +95,46 @@ def test_bpe_encode_decode_match_reference(ref, built_lib, chip_dir):
         # max_tokens truncation
         assert chip.encode(TEXTS[3], 5).tolist() == ref.encode(h, TEXTS[3], 5).tolist()
     ref.L.refh_chip_destroy(h)
+
+
+def test_fused_plan_matches_compiler_tapes(built_lib, chip_dir):
+    import kmap_b200
+    for name in ("gqa", "mha", "tl"):
+        with kmap_b200.Chip(chip_dir(name)) as chip:
+            ok, why = chip.plan_match()
+            assert ok, (name, why)
+
+
+def test_fused_plan_rejects_changed_tapes(built_lib, chip_dir):
+    """Any change to the template's wiring or parameters sends processor_infer
+    to the per-instruction executor instead of the fused plan."""
+    import ctypes as C
+
+    import kmap_b200
+    from kmap_b200 import chipgen
+    with kmap_b200.Chip(chip_dir("tl")) as chip:
+        lib = kmap_b200.lib()
+        n = chip.info["n_instrs"]
+        edits = [(3, "axis", 0), (3, "keepdims", 0), (12, "in0", 3), (n - 1, "in1", 0),
+                 (30, "tag", 8), (9, "starts", 1)]
+        for i, field, val in edits:
+            p = lib.tape_get_instr(chip.ctx, i)
+            rec = np.frombuffer(C.string_at(p, 276), chipgen.INSTR_DTYPE).copy()
+            old = np.copy(rec[0][field])
+            if np.ndim(old):
+                rec[0][field][1] = old[1] + val
+            else:
+                rec[0][field] = val if old != val else val + 1
+            C.memmove(p, rec.ctypes.data, 276)
+            ok, why = chip.plan_match()
+            assert not ok and why, (i, field)
+            rec[0][field] = old
+            C.memmove(p, rec.ctypes.data, 276)
+        assert chip.plan_match()[0]
+        # a KV output that differs from the slot map
+        import json
+        import os
+        m = json.load(open(os.path.join(chip.path, "processor.json")))
+        ko = [m["output_map"]["L%d/new_%s" % (l, c)] for l in range(2) for c in "kv"]
+        ko[1], ko[0] = ko[0], ko[1]
+        assert not chip.plan_match(kv_out=ko)[0]
