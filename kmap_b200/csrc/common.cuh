@@ -76,6 +76,7 @@ struct CtxImpl {
     // GEMV scratch: ordered partial sums [T][rows][N]
     float *d_part = nullptr;
     size_t part_cap = 0;
+    int *d_counters = nullptr;   // fused TT-GEMV arrival counters (zero at rest)
     // fused decode path
     DecodePlan *plan = nullptr;
     kllm_infer_opts opts;
@@ -119,6 +120,11 @@ bool tt_gemv_partials(cudaStream_t s, const float *x, int rows, const float *cb,
                       int n_codes, const uint16_t *idx, int K, int N, float *part);
 bool tt_reduce_partials(cudaStream_t s, const float *part, int T, int rows, int N,
                         float *y);
+// One-row TT-GEMV with the ordered reduction fused; false (no error) when
+// the matrix does not meet the TMA rules.
+bool tt_gemv_fused_y(cudaStream_t s, const float *x, const float *cb, int n_codes,
+                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y);
+bool tt_fused_applies(const uint16_t *idx, const float *cb, int K, int N, int n_codes);
 
 extern long long g_launches;   // kernels launched by this process
 

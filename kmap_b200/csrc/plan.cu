@@ -3,18 +3,17 @@
 // processor_infer drives one tape step per token (reference
 // _tape_runner.c:1602-1763).  When the tape is exactly the template the
 // kllm compiler emits (kllm_compile.c:1143-1385 per layer, driven by
-// :1427-1690), the plan replaces its ~60 instructions per layer by 7 fused
-// kernels over device-resident state:
+// :1427-1690), the plan replaces its ~60 instructions per layer by 5 fused
+// kernels over device-resident state (tt_fused.cuh for the TT-GEMVs):
 //
-//   resid_norm   h = embed[token] | h + sum_t part[t];  xn = rmsnorm(h) * w
-//   ttgemv       QKV partials                        (TMA, exact order)
-//   attention    RoPE(q,k), KV append in place, softmax(q.K^T * scale).V
-//   ttgemv       O partials
-//   resid_norm   h += O;  xn = rmsnorm(h) * w2
-//   ttgemv       gate_up partials
-//   ttgemv       down partials, x = silu(gate) * up fused into its load
-// then final resid_norm, the lm_head TT-GEMV and a multi-CTA logits +
-// first-maximum argmax that feeds the next step's embedding lookup.
+//   qkv        x = rmsnorm(h) * w1 (h = embedding row in layer 0), TT-GEMV
+//   attention  RoPE(q,k), KV append in place, softmax(q.K^T * scale).V
+//   o          TT-GEMV of the attention output, h += y
+//   gate_up    x = rmsnorm(h) * w2, TT-GEMV, act = silu(gate) * up
+//   down       TT-GEMV of act, h += y
+// then the lm_head TT-GEMV (final rmsnorm in its prologue) whose epilogue
+// forms the logits and the first-maximum argmax that feeds the next step's
+// embedding lookup.
 //
 // Arithmetic follows the tape op for op: every elementwise step is the
 // same float operation (no FMA contraction), SILU / EXP / RSQRT evaluate in
@@ -36,15 +35,10 @@
 
 #include "plan.cuh"
 #include "sm100.cuh"
-#include "tt_kernels.cuh"
+#include "tt_fused.cuh"
 
 namespace kllm {
 
-bool tt_gemv_tma_plain(cudaStream_t s, const CUtensorMap &map, const float *x, const float *cb,
-                       int n_codes, int K, int N, float *part, int *status, bool pdl);
-bool tt_gemv_tma_swiglu(cudaStream_t s, const CUtensorMap &map, const float *gu_part, int T_gu,
-                        int F, const float *cb, int n_codes, int K, int N, float *part,
-                        int *status, bool pdl);
 
 // ============================================================ matching ===
 
@@ -347,68 +341,6 @@ static bool match_template(const TapeCtx *ctx, const PlanDesc &d, TemplateInfo *
 
 // ============================================================= kernels ===
 
-struct StepState {
-    int pos;          // position of the token fed this step
-    int prompt_len;
-    int n_gen;        // tokens generated so far
-    int counter;      // argmax CTA arrival counter
-};
-
-// h = embed row of this step's token (mode 0) or h + sum_t part[t]
-// (mode 1); xn = rmsnorm(h) * w  (kllm_compile.c:1143-1164: MUL, MEAN,
-// ADD eps, RSQRT in double, MUL, MUL).  One CTA; the sum of squares is a
-// fixed-shape tree, the rest is the tape's float arithmetic.
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS)
-k_resid_norm(int mode, const float *__restrict__ embed, const StepState *st,
-             const int *__restrict__ prompt, const int *__restrict__ gen, int V,
-             const float *__restrict__ part, int T, float *__restrict__ h, int H,
-             const float *__restrict__ w, float eps, float inv_h, float *__restrict__ xn,
-             int *status) {
-    __shared__ float red[THREADS / 32];
-    __shared__ float s_rsq;
-    pdl_launch_dependents();
-    pdl_wait();
-    const float *src = nullptr;
-    if (mode == 0) {
-        int pos = st->pos, P = st->prompt_len;
-        int tok = pos < P ? prompt[pos] : gen[pos - P];
-        if (tok < 0 || tok >= V) {
-            if (threadIdx.x == 0) atomicOr(status, ST_BAD_TOKEN);
-            tok = 0;
-        }
-        src = embed + (size_t)tok * H;
-    }
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += THREADS) {
-        float v;
-        if (mode == 0) {
-            v = src[i];
-        } else {
-            float a = part[i];
-            for (int t = 1; t < T; t++) a = __fadd_rn(a, part[(size_t)t * H + i]);
-            v = __fadd_rn(h[i], a);
-        }
-        h[i] = v;
-        ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < THREADS / 32 ? red[threadIdx.x] : 0.f;
-        for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (threadIdx.x == 0) {
-            float mean = __fmul_rn(v, inv_h);
-            float add = __fadd_rn(mean, eps);
-            s_rsq = (float)(1.0 / sqrt((double)add));
-        }
-    }
-    __syncthreads();
-    const float r = s_rsq;
-    for (int i = threadIdx.x; i < H; i += THREADS) xn[i] = __fmul_rn(__fmul_rn(h[i], r), w[i]);
-}
-
 // Attention for one query head (kllm_compile.c:1216-1343 after the QKV
 // projection): ordered chunk sums of the QKV partials, RoPE of q and k,
 // append of k/v at `pos` (by the first query head of each KV group),
@@ -521,87 +453,6 @@ k_attention(const StepState *st, const float *__restrict__ qkv_part, int T, int 
     }
 }
 
-// logits[v] = ordered chunk sum of the lm_head partials, then the
-// first-maximum argmax across CTAs (_tape_runner.c:1717-1727); the last CTA
-// to finish publishes the token and advances the step.
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS)
-k_logits_argmax(StepState *st, const float *__restrict__ part, int T, int V,
-                float *__restrict__ logits, float *__restrict__ hist, int hist_rows,
-                float *__restrict__ cand_v, int *__restrict__ cand_i, int *__restrict__ gen,
-                volatile int *gen_host, int max_gen) {
-    __shared__ float rv[THREADS / 32];
-    __shared__ int ri[THREADS / 32];
-    __shared__ bool last;
-    pdl_launch_dependents();
-    pdl_wait();
-    const int pos = st->pos;
-    const int per = (V + gridDim.x - 1) / gridDim.x;
-    const int v0 = blockIdx.x * per, v1 = min(V, v0 + per);
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = v0 + threadIdx.x; i < v1; i += THREADS) {
-        float a = part[i];
-        for (int t = 1; t < T; t++) a = __fadd_rn(a, part[(size_t)t * V + i]);
-        logits[i] = a;
-        if (hist && pos < hist_rows) hist[(size_t)pos * V + i] = a;
-        if (a > bv || (a == bv && i < bi) || bi == 0x7fffffff) {
-            bv = a;
-            bi = i;
-        }
-    }
-    for (int o = 16; o; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        rv[threadIdx.x >> 5] = bv;
-        ri[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < THREADS / 32; w++)
-            if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) {
-                bv = rv[w];
-                bi = ri[w];
-            }
-        cand_v[blockIdx.x] = bv;
-        cand_i[blockIdx.x] = bi;
-        __threadfence();
-        last = atomicAdd(&st->counter, 1) == (int)gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!last || threadIdx.x != 0) return;
-    __threadfence();
-    float best = cand_v[0];
-    int bidx = cand_i[0];
-    for (int b = 1; b < (int)gridDim.x; b++) {
-        float cv = ((volatile float *)cand_v)[b];
-        int ci = ((volatile int *)cand_i)[b];
-        if (cv > best || (cv == best && ci < bidx)) {
-            best = cv;
-            bidx = ci;
-        }
-    }
-    if (bidx < 0 || bidx >= V) bidx = 0;
-    const int P = st->prompt_len;
-    if (pos >= P - 1) {
-        int gi = pos - (P - 1);
-        if (gi < max_gen) {
-            gen[gi] = bidx;
-            gen_host[gi] = bidx;
-            __threadfence_system();
-        }
-        st->n_gen = gi + 1;
-    }
-    st->counter = 0;
-    st->pos = pos + 1;
-}
-
 // ================================================================ plan ===
 
 struct DecodePlan {
@@ -612,8 +463,9 @@ struct DecodePlan {
     const float *src_cos = nullptr, *src_sin = nullptr;
     // device state
     float *embed = nullptr, *rcos = nullptr, *rsin = nullptr;
-    float *h = nullptr, *xn = nullptr, *ctx = nullptr, *logits = nullptr;
-    float *p_qkv = nullptr, *p_o = nullptr, *p_gu = nullptr, *p_dn = nullptr, *p_lm = nullptr;
+    float *h = nullptr, *qkv = nullptr, *ctx = nullptr, *act = nullptr, *logits = nullptr;
+    float *part = nullptr;          // [T][N] chunk partials, shared by the GEMVs
+    int *counters = nullptr;        // column-block arrival counters (zero at rest)
     float *kc = nullptr, *vc = nullptr;
     float *cand_v = nullptr;
     int *cand_i = nullptr;
@@ -628,12 +480,13 @@ struct DecodePlan {
     std::vector<float> eps;
     float scale = 0.f, f_eps = 0.f;
     std::vector<CUtensorMap> maps;   // per layer: qkv, o, gu, dn ; then lm
+    std::vector<TFConfig> cfgs;      // launch geometry per map
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     float *graph_hist = nullptr;   // history buffer baked into the graph
+    long long kernels_per_step = 0;
     int graph_hist_rows = 0;
     int logits_slot = -1;
-    int argmax_ctas = 148;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
     std::vector<cudaEvent_t> step_ev;
 };
@@ -642,8 +495,8 @@ static void free_plan(DecodePlan *p) {
     if (!p) return;
     if (p->exec) cudaGraphExecDestroy(p->exec);
     if (p->graph) cudaGraphDestroy(p->graph);
-    void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->xn, p->ctx, p->logits, p->p_qkv,
-                    p->p_o, p->p_gu, p->p_dn, p->p_lm, p->kc, p->vc, p->cand_v, p->cand_i,
+    void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->qkv, p->ctx, p->act, p->logits,
+                    p->part, p->counters, p->kc, p->vc, p->cand_v, p->cand_i,
                     p->st, p->prompt, p->gen, p->status, p->hist};
     for (void *b : bufs)
         if (b) cudaFree(b);
@@ -689,6 +542,12 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         *why = "head_dim " + std::to_string(ti.hd) + " (fused attention covers 32, 64, 128)";
         return false;
     }
+    if (ti.F % 8 != 0) {
+        // the up half of each gate_up tile starts at column F: a TMA x
+        // coordinate must be a multiple of 8 uint16
+        *why = "intermediate size not a multiple of 8";
+        return false;
+    }
     if ((size_t)max_pos * 4 > 160 * 1024) {
         *why = "context longer than the fused attention's score buffer";
         return false;
@@ -725,16 +584,22 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     for (int s : tts) {
         if (!upload_tt(c, s)) return fail();
         const Slot &sl = ctx->slots[s];
-        if (!tt_tma_ok(c->ds[s].d_idx, sl.tt_K, sl.tt_N, sl.n_codes)) {
+        (void)sl;
+    }
+    p->maps.resize(tts.size());
+    p->cfgs.resize(tts.size());
+    for (size_t i = 0; i < tts.size(); i++) {
+        const Slot &sl = ctx->slots[tts[i]];
+        const int em = (i + 1 == tts.size()) ? E_ARGMAX : (i % 4 == 2 ? E_SWIGLU : E_Y);
+        p->cfgs[i] = tf_config(sl.tt_K, sl.tt_N, sl.n_codes, em);
+        if (!tf_tma_ok(c->ds[tts[i]].d_idx, c->ds[tts[i]].d_cb, sl.tt_K, sl.tt_N, sl.n_codes,
+                       p->cfgs[i])) {
             *why = "a weight matrix does not meet the TMA alignment rules";
             free_plan(p);
             return false;
         }
-    }
-    p->maps.resize(tts.size());
-    for (size_t i = 0; i < tts.size(); i++) {
-        const Slot &sl = ctx->slots[tts[i]];
-        if (!make_idx_tmap(&p->maps[i], c->ds[tts[i]].d_idx, sl.tt_K, sl.tt_N, 128, 32))
+        if (!make_idx_tmap(&p->maps[i], c->ds[tts[i]].d_idx, sl.tt_K, sl.tt_N,
+                           p->cfgs[i].bw(), 32))
             return fail();
     }
     // norm weights and constants
@@ -771,16 +636,29 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         return fail();
     // activations, partials, KV cache, step state
     size_t kv = (size_t)L * nkv * max_pos * hd;
-    if (!dalloc(&p->h, H) || !dalloc(&p->xn, std::max(H, F)) || !dalloc(&p->ctx, qd) ||
-        !dalloc(&p->logits, V) || !dalloc(&p->p_qkv, (size_t)p->T_h * nq) ||
-        !dalloc(&p->p_o, (size_t)p->T_qd * H) || !dalloc(&p->p_gu, (size_t)p->T_h * 2 * F) ||
-        !dalloc(&p->p_dn, (size_t)p->T_f * H) || !dalloc(&p->p_lm, (size_t)p->T_h * V) ||
-        !dalloc(&p->kc, kv) || !dalloc(&p->vc, kv) || !dalloc(&p->cand_v, 1024) ||
-        !dalloc(&p->cand_i, 1024) || !dalloc(&p->st, 1) || !dalloc(&p->prompt, max_pos) ||
-        !dalloc(&p->gen, max_pos) || !dalloc(&p->status, 1))
+    size_t part_n = std::max({(size_t)p->T_h * nq, (size_t)p->T_qd * H, (size_t)p->T_h * 2 * F,
+                              (size_t)p->T_f * H, (size_t)p->T_h * V});
+    const int n_cnt = 4096;
+    int nblk = 0;
+    for (size_t i = 0; i < tts.size(); i++) {
+        const Slot &sl = ctx->slots[tts[i]];
+        const int em = (i + 1 == tts.size()) ? E_ARGMAX : (i % 4 == 2 ? E_SWIGLU : E_Y);
+        nblk = std::max(nblk, tf_blocks(p->cfgs[i], sl.tt_N, sl.tt_N / 2, em));
+    }
+    if (nblk > 1024 || nblk > n_cnt) {
+        *why = "too many column blocks for the argmax candidates";
+        free_plan(p);
+        return false;
+    }
+    if (!dalloc(&p->h, H) || !dalloc(&p->qkv, nq) || !dalloc(&p->ctx, qd) ||
+        !dalloc(&p->act, F) || !dalloc(&p->logits, V) || !dalloc(&p->part, part_n) ||
+        !dalloc(&p->counters, n_cnt) || !dalloc(&p->kc, kv) || !dalloc(&p->vc, kv) ||
+        !dalloc(&p->cand_v, 1024) || !dalloc(&p->cand_i, 1024) || !dalloc(&p->st, 1) ||
+        !dalloc(&p->prompt, max_pos) || !dalloc(&p->gen, max_pos) || !dalloc(&p->status, 1))
         return fail();
     if (!KLLM_CUDA(cudaMemset(p->kc, 0, kv * 4)) || !KLLM_CUDA(cudaMemset(p->vc, 0, kv * 4)) ||
-        !KLLM_CUDA(cudaMemset(p->st, 0, sizeof(StepState))))
+        !KLLM_CUDA(cudaMemset(p->st, 0, sizeof(StepState))) ||
+        !KLLM_CUDA(cudaMemset(p->counters, 0, n_cnt * sizeof(int))))
         return fail();
     if (!KLLM_CUDA(cudaHostAlloc((void **)&p->gen_host, (size_t)max_pos * 4,
                                  cudaHostAllocMapped)) ||
@@ -789,9 +667,6 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     if (!KLLM_CUDA(cudaEventCreate(&p->ev0)) || !KLLM_CUDA(cudaEventCreate(&p->ev1)) ||
         !KLLM_CUDA(cudaEventCreate(&p->ev2)))
         return fail();
-    int argc = 148;
-    cudaDeviceGetAttribute(&argc, cudaDevAttrMultiProcessorCount, c->device);
-    p->argmax_ctas = std::min(std::max(1, (V + 255) / 256), std::min(argc, 1024));
     c->plan = p;
     return true;
 }
@@ -819,62 +694,75 @@ static bool record_step(CtxImpl *c, DecodePlan *p) {
     const TemplateInfo &t = p->ti;
     const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, nq = qd + 2 * nkv * hd;
     const int F = t.F, V = t.V;
-    const float inv_h = 1.0f / (float)H;
     const TapeCtx *ctx = &c->base;
-    constexpr int NT = 1024;
+    auto gemv = [&](int mi, int w_slot, int K, int N, int xmode, const float *x, int norm_i,
+                    float eps, bool embed, int emode, float *y) -> bool {
+        const DevSlot &w = c->ds[w_slot];
+        TTArgs a = {};
+        a.cb = w.d_cb;
+        a.n_codes = ctx->slots[w_slot].n_codes;
+        a.K = K;
+        a.N = N;
+        a.T = tt_chunks(K);
+        a.F = F;
+        a.xmode = xmode;
+        a.x = x;
+        a.norm_w = norm_i >= 0 ? p->dev_norm[norm_i] : nullptr;
+        a.eps = eps;
+        a.inv_k = 1.0f / (float)K;
+        if (embed) {
+            a.embed = p->embed;
+            a.h_init = p->h;
+        }
+        a.st = p->st;
+        a.prompt = p->prompt;
+        a.gen = p->gen;
+        a.vocab = V;
+        a.emode = emode;
+        a.part = p->part;
+        a.counters = p->counters;
+        a.y = y;
+        a.logits = p->logits;
+        a.hist = p->hist;
+        a.hist_rows = p->hist_rows;
+        a.cand_v = p->cand_v;
+        a.cand_i = p->cand_i;
+        a.stw = p->st;
+        a.gen_dev = p->gen;
+        a.gen_host = (volatile int *)p->gen_host_dev;
+        a.max_gen = p->max_pos;
+        a.status = p->status;
+        return launch_tt_fused(s, p->cfgs[mi], p->maps[mi], a, true);
+    };
     for (int l = 0; l < t.L; l++) {
         const LayerSlots &ls = t.layers[l];
-        const DevSlot &wq = c->ds[ls.qkv], &wo = c->ds[ls.o], &wg = c->ds[ls.gu],
-                      &wd = c->ds[ls.dn];
-        // residual (from the previous layer's down projection) + norm 1
-        if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, l == 0 ? 0 : 1,
-                        (const float *)p->embed, (const StepState *)p->st, (const int *)p->prompt,
-                        (const int *)p->gen, V, (const float *)p->p_dn, p->T_f, p->h, H,
-                        (const float *)p->dev_norm[2 * l], p->eps[2 * l], inv_h, p->xn,
-                        p->status))
-            return false;
-        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 0], p->xn, wq.d_cb, ctx->slots[ls.qkv].n_codes,
-                               H, nq, p->p_qkv, p->status, true))
+        // x = rmsnorm(h) * w1 (the embedding row in layer 0) -> qkv
+        if (!gemv(4 * l + 0, ls.qkv, H, nq, X_NORM, p->h, 2 * l, p->eps[2 * l], l == 0, E_Y,
+                  p->qkv))
             return false;
         size_t smem_att = (size_t)p->max_pos * 4;
         auto att = hd == 32 ? k_attention<32, 256> : hd == 64 ? k_attention<64, 256>
                                                               : k_attention<128, 256>;
         if (!launch_pdl(s, att, dim3(t.nh), dim3(256), smem_att, (const StepState *)p->st,
-                        (const float *)p->p_qkv, p->T_h, nq, (const float *)p->rcos,
+                        (const float *)p->qkv, 1, nq, (const float *)p->rcos,
                         (const float *)p->rsin, p->kc + (size_t)l * nkv * p->max_pos * hd,
                         p->vc + (size_t)l * nkv * p->max_pos * hd, p->max_pos, t.groups, nkv,
                         p->scale, p->ctx))
             return false;
-        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 1], p->ctx, wo.d_cb, ctx->slots[ls.o].n_codes,
-                               qd, H, p->p_o, p->status, true))
+        // h += ctx @ Wo
+        if (!gemv(4 * l + 1, ls.o, qd, H, X_PLAIN, p->ctx, -1, 0.f, false, E_RESID, p->h))
             return false;
-        if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, 1, (const float *)p->embed,
-                        (const StepState *)p->st, (const int *)p->prompt, (const int *)p->gen, V,
-                        (const float *)p->p_o, p->T_qd, p->h, H,
-                        (const float *)p->dev_norm[2 * l + 1], p->eps[2 * l + 1], inv_h, p->xn,
-                        p->status))
+        // x = rmsnorm(h) * w2 -> act = silu(gate) * up
+        if (!gemv(4 * l + 2, ls.gu, H, 2 * F, X_NORM, p->h, 2 * l + 1, p->eps[2 * l + 1], false,
+                  E_SWIGLU, p->act))
             return false;
-        if (!tt_gemv_tma_plain(s, p->maps[4 * l + 2], p->xn, wg.d_cb, ctx->slots[ls.gu].n_codes,
-                               H, 2 * F, p->p_gu, p->status, true))
-            return false;
-        if (!tt_gemv_tma_swiglu(s, p->maps[4 * l + 3], p->p_gu, p->T_h, F, wd.d_cb,
-                                ctx->slots[ls.dn].n_codes, F, H, p->p_dn, p->status, true))
+        // h += act @ Wdown
+        if (!gemv(4 * l + 3, ls.dn, F, H, X_PLAIN, p->act, -1, 0.f, false, E_RESID, p->h))
             return false;
     }
-    if (!launch_pdl(s, k_resid_norm<NT>, dim3(1), dim3(NT), 0, 1, (const float *)p->embed,
-                    (const StepState *)p->st, (const int *)p->prompt, (const int *)p->gen, V,
-                    (const float *)p->p_dn, p->T_f, p->h, H, (const float *)p->dev_norm.back(),
-                    p->f_eps, inv_h, p->xn, p->status))
-        return false;
-    const DevSlot &wl = c->ds[t.lm];
-    if (!tt_gemv_tma_plain(s, p->maps.back(), p->xn, wl.d_cb, ctx->slots[t.lm].n_codes, H, V,
-                           p->p_lm, p->status, true))
-        return false;
-    if (!launch_pdl(s, k_logits_argmax<256>, dim3(p->argmax_ctas), dim3(256), 0, p->st,
-                    (const float *)p->p_lm, p->T_h, V, p->logits, p->hist, p->hist_rows,
-                    p->cand_v, p->cand_i, p->gen, (volatile int *)p->gen_host_dev, p->max_pos))
-        return false;
-    return true;
+    // logits = rmsnorm(h) * wf @ Wlm, greedy token
+    return gemv((int)p->maps.size() - 1, t.lm, H, V, X_NORM, p->h, 2 * t.L, p->f_eps, false,
+                E_ARGMAX, nullptr);
 }
 
 static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
@@ -885,7 +773,10 @@ static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
     p->graph = nullptr;
     if (!KLLM_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal)))
         return false;
+    long long l0 = g_launches;
     bool ok = record_step(c, p);
+    p->kernels_per_step = g_launches - l0;
+    g_launches = l0;   // counted when the graph is replayed
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (!ok || !KLLM_CUDA(e)) {
@@ -948,7 +839,13 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
                 return false;
     }
     auto launch_step = [&](int i) -> bool {
-        bool ok = graphs ? KLLM_CUDA(cudaGraphLaunch(p->exec, s)) : record_step(c, p);
+        bool ok;
+        if (graphs) {
+            ok = KLLM_CUDA(cudaGraphLaunch(p->exec, s));
+            g_launches += p->kernels_per_step;
+        } else {
+            ok = record_step(c, p);
+        }
         return ok && KLLM_CUDA(cudaEventRecord(p->step_ev[i], s));
     };
     if (!KLLM_CUDA(cudaEventRecord(p->ev0, s))) return false;

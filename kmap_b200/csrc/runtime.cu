@@ -272,6 +272,7 @@ void tape_ctx_destroy(TapeCtx *ctx) {
     }
     if (c->stream) {
         if (c->d_part) cudaFreeAsync(c->d_part, c->stream);
+        if (c->d_counters) cudaFreeAsync(c->d_counters, c->stream);
         cudaStreamSynchronize(c->stream);
         cudaStreamDestroy(c->stream);
     }
@@ -638,6 +639,21 @@ bool run_generic(CtxImpl *c) {
             int T = tt_chunks(K);
             if (!ensure_part(c, (size_t)T * rows * N)) return false;
             const DevSlot &w = c->ds[op->in1];
+            if (rows == 1 && tt_fused_applies(w.d_idx, w.d_cb, K, N, s1->n_codes)) {
+                if (!c->d_counters) {
+                    if (!KLLM_CUDA(cudaMallocAsync((void **)&c->d_counters, 4096 * 4, st)) ||
+                        !KLLM_CUDA(cudaMemsetAsync(c->d_counters, 0, 4096 * 4, st)))
+                        return false;
+                }
+                if (N / 64 + 1 > 4096) {
+                    set_error("instruction %d: MATMUL_TT wider than the counter table", i);
+                    return false;
+                }
+                if (!tt_gemv_fused_y(st, D(c, op->in0), w.d_cb, s1->n_codes, w.d_idx, K, N,
+                                     c->d_part, c->d_counters, D(c, o)))
+                    return false;
+                break;
+            }
             if (!tt_gemv_partials(st, D(c, op->in0), rows, w.d_cb, s1->n_codes, w.d_idx, K, N,
                                   c->d_part))
                 return false;

@@ -18,12 +18,13 @@
 // one (indices straight from HBM, codebook through the read-only cache) for
 // everything else.
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
-#include "tt_kernels.cuh"
+#include "tt_fused.cuh"
 
 namespace kllm {
 
@@ -98,27 +99,55 @@ __global__ void k_tt_gemv_simple(const float *__restrict__ x, int rows,
     }
 }
 
-// Decode-shape configuration of the TMA kernel: 2 consumer warps x 2
-// columns per lane = 128 columns per CTA, 32-row boxes (8 KB), up to 8
-// stages in flight.
-constexpr int kNCW = 2, kCPL = 2, kBR = 32, kMaxStages = 8;
-using Geo = TTGeom<kNCW, kCPL, kBR>;
+// ------------------------------------------------------ fused kernel ----
 
-int tt_tma_stages(int n_codes, int len) {
-    int nbox = (len + kBR - 1) / kBR;
-    int ns = std::min(kMaxStages, std::max(nbox, 1));
-    while (ns > 2 && tt_smem_bytes<kNCW, kCPL, kBR>(n_codes, len, ns) > 110 * 1024) ns--;
-    return ns;
+static int env_int(const char *name, int dflt) {
+    const char *v = getenv(name);
+    return v && *v ? atoi(v) : dflt;
 }
 
-template <class XS>
-static bool launch_tma(cudaStream_t s, const CUtensorMap &map, const float *cb, int n_codes,
-                       const XS &xs, int K, int N, float *part, int *status, bool pdl) {
-    int T = tt_chunks(K);
-    int maxlen = (K + T - 1) / T;
-    int ns = tt_tma_stages(n_codes, maxlen);
-    size_t smem = tt_smem_bytes<kNCW, kCPL, kBR>(n_codes, maxlen, ns);
-    auto kern = k_ttgemv_tma<kNCW, kCPL, kBR, XS>;
+// Geometry heuristic.  Every (column, chunk) chain is serial, so a matrix
+// with few columns has few chains: it gets one column per lane and four
+// consumer warps per 128 columns (many warps to hide the gather latency).
+// Wide matrices are bound by shared-memory wavefronts instead: two or four
+// columns per lane halve the index reads.  KLLM_TT_CPL / KLLM_TT_STAGES
+// override for tuning.
+TFConfig tf_config(int K, int N, int n_codes, int emode) {
+    (void)K;
+    (void)n_codes;
+    TFConfig c;
+    c.ncw = 4;
+    c.nsub = emode == E_SWIGLU ? 2 : 1;
+    long long cols = emode == E_SWIGLU ? N / 2 : N;
+    c.cpl = cols >= 8192 ? 2 : 1;
+    c.stages = 2;
+    int e = env_int("KLLM_TT_CPL", 0);
+    if (e == 1 || e == 2 || e == 4) c.cpl = e;
+    e = env_int("KLLM_TT_STAGES", 0);
+    if (e >= 1 && e <= 16) c.stages = e;
+    return c;
+}
+
+int tf_blocks(const TFConfig &c, int N, int F, int emode) {
+    return emode == E_SWIGLU ? (F + c.bw() - 1) / c.bw() : (N + c.bn() - 1) / c.bn();
+}
+
+bool tf_tma_ok(const uint16_t *idx, const float *cb, int K, int N, int n_codes,
+               const TFConfig &c) {
+    return K > 0 && N >= 8 && (N % 8) == 0 && ((uintptr_t)idx % 16) == 0 &&
+           ((uintptr_t)cb % 16) == 0 && n_codes <= 16384 && c.bw() % 8 == 0;
+}
+
+template <int NCW, int CPL, int NSUB>
+static bool launch_g(cudaStream_t s, const TFConfig &c, const CUtensorMap &map, TTArgs a,
+                     bool pdl) {
+    constexpr int BR = 32;
+    using G = TFGeom<NCW, CPL, BR, NSUB>;
+    int maxlen = (a.K + a.T - 1) / a.T;
+    int nbox = (maxlen + BR - 1) / BR;
+    a.stages = std::max(1, std::min(c.stages, nbox));
+    size_t smem = tf_smem_bytes<NCW, CPL, BR, NSUB>(a.n_codes, maxlen, a.stages);
+    auto kern = k_tt_fused<NCW, CPL, BR, NSUB>;
     static bool attr_set[64] = {};
     int dev = 0;
     if (!KLLM_CUDA(cudaGetDevice(&dev))) return false;
@@ -129,8 +158,8 @@ static bool launch_tma(cudaStream_t s, const CUtensorMap &map, const float *cb, 
         attr_set[dev & 63] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((N + Geo::BN - 1) / Geo::BN, T);
-    cfg.blockDim = dim3(Geo::THREADS);
+    cfg.gridDim = dim3(tf_blocks(c, a.N, a.F, a.emode), a.T);
+    cfg.blockDim = dim3(G::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute at[1];
@@ -139,35 +168,62 @@ static bool launch_tma(cudaStream_t s, const CUtensorMap &map, const float *cb, 
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
     g_launches++;
-    return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, map, cb, n_codes, xs, K, N, T, ns, part,
-                                        status));
+    return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, map, a));
 }
 
-bool tt_gemv_tma_plain(cudaStream_t s, const CUtensorMap &map, const float *x, const float *cb,
-                       int n_codes, int K, int N, float *part, int *status, bool pdl) {
-    return launch_tma(s, map, cb, n_codes, XPlain{x}, K, N, part, status, pdl);
-}
-
-// x = silu(gate) * up from the gate_up projection's T_gu partial rows.
-bool tt_gemv_tma_swiglu(cudaStream_t s, const CUtensorMap &map, const float *gu_part, int T_gu,
-                        int F, const float *cb, int n_codes, int K, int N, float *part,
-                        int *status, bool pdl) {
-    XSwiGLU xs{gu_part, T_gu, F, 2LL * F};
-    return launch_tma(s, map, cb, n_codes, xs, K, N, part, status, pdl);
+bool launch_tt_fused(cudaStream_t s, const TFConfig &c, const CUtensorMap &map, TTArgs a,
+                     bool pdl) {
+    if (c.ncw != 4) {
+        set_error("unsupported TT-GEMV geometry");
+        return false;
+    }
+    if (c.nsub == 1) {
+        if (c.cpl == 1) return launch_g<4, 1, 1>(s, c, map, a, pdl);
+        if (c.cpl == 2) return launch_g<4, 2, 1>(s, c, map, a, pdl);
+        if (c.cpl == 4) return launch_g<4, 4, 1>(s, c, map, a, pdl);
+    } else if (c.nsub == 2) {
+        if (c.cpl == 1) return launch_g<4, 1, 2>(s, c, map, a, pdl);
+        if (c.cpl == 2) return launch_g<4, 2, 2>(s, c, map, a, pdl);
+    }
+    set_error("unsupported TT-GEMV geometry");
+    return false;
 }
 
 bool tt_gemv_partials(cudaStream_t s, const float *x, int rows, const float *cb, int n_codes,
                       const uint16_t *idx, int K, int N, float *part) {
     int T = tt_chunks(K);
-    if (rows == 1 && tt_tma_ok(idx, K, N, n_codes)) {
-        CUtensorMap map;
-        if (!make_idx_tmap(&map, idx, K, N, Geo::BN, kBR)) return false;
-        return tt_gemv_tma_plain(s, map, x, cb, n_codes, K, N, part, nullptr, false);
-    }
     dim3 grid((N + 127) / 128, T);
     k_tt_gemv_simple<<<grid, 128, 0, s>>>(x, rows, cb, idx, K, N, T, part);
     g_launches++;
     return KLLM_CUDA(cudaGetLastError());
+}
+
+bool tt_fused_applies(const uint16_t *idx, const float *cb, int K, int N, int n_codes) {
+    return tf_tma_ok(idx, cb, K, N, n_codes, tf_config(K, N, n_codes, E_Y));
+}
+
+// Single-row TT-GEMV with the reduction fused (the fast path of the tape's
+// MATMUL_TT and of kllm_tt_gemv): part holds T*N floats, counters
+// tf_blocks() zeros (left zero again).
+bool tt_gemv_fused_y(cudaStream_t s, const float *x, const float *cb, int n_codes,
+                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y) {
+    TFConfig c = tf_config(K, N, n_codes, E_Y);
+    if (!tf_tma_ok(idx, cb, K, N, n_codes, c)) return false;
+    CUtensorMap map;
+    if (!make_idx_tmap(&map, idx, K, N, c.bw(), 32)) return false;
+    TTArgs a = {};
+    a.cb = cb;
+    a.n_codes = n_codes;
+    a.K = K;
+    a.N = N;
+    a.T = tt_chunks(K);
+    a.xmode = X_PLAIN;
+    a.x = x;
+    a.emode = E_Y;
+    a.part = part;
+    a.counters = counters;
+    a.y = y;
+    return launch_tt_fused(s, c, map, a, false);
 }
 
 // y = ((p0 + p1) + p2) + ...  (memcpy of chunk 0, then in-order adds)
@@ -191,25 +247,40 @@ bool tt_reduce_partials(cudaStream_t s, const float *part, int T, int rows, int 
 }
 
 // ---------------------------------------------------------- raw C ABI ----
-// Per-device scratch for the chunk partials of kllm_tt_gemv.
+// Per-device scratch of kllm_tt_gemv: chunk partials and the column-block
+// arrival counters of the fused reduction (kept zero between calls).
 struct GemvScratch {
     float *part = nullptr;
     size_t cap = 0;
+    int *counters = nullptr;
+    size_t ccap = 0;
 };
 static std::mutex g_scratch_mu;
 static GemvScratch g_scratch[64];
 
-static float *scratch_for(int dev, size_t floats) {
+static bool scratch_for(int dev, size_t floats, size_t ncount, float **part, int **counters) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     GemvScratch &s = g_scratch[dev & 63];
     if (s.cap < floats) {
         if (s.part) cudaFree(s.part);
         s.part = nullptr;
         s.cap = 0;
-        if (!KLLM_CUDA(cudaMalloc((void **)&s.part, floats * sizeof(float)))) return nullptr;
+        if (!KLLM_CUDA(cudaMalloc((void **)&s.part, floats * sizeof(float)))) return false;
         s.cap = floats;
     }
-    return s.part;
+    if (s.ccap < ncount) {
+        if (s.counters) cudaFree(s.counters);
+        s.counters = nullptr;
+        s.ccap = 0;
+        size_t n = std::max<size_t>(ncount, 1024);
+        if (!KLLM_CUDA(cudaMalloc((void **)&s.counters, n * sizeof(int))) ||
+            !KLLM_CUDA(cudaMemset(s.counters, 0, n * sizeof(int))))
+            return false;
+        s.ccap = n;
+    }
+    *part = s.part;
+    *counters = s.counters;
+    return true;
 }
 
 }  // namespace kllm
@@ -230,8 +301,11 @@ extern "C" int kllm_tt_gemv(const float *x, int rows, const float *codebook, int
     int dev = 0;
     if (!KLLM_CUDA(cudaGetDevice(&dev))) return -1;
     int T = tt_chunks(K);
-    float *part = scratch_for(dev, (size_t)T * rows * N);
-    if (!part) return -1;
+    float *part = nullptr;
+    int *counters = nullptr;
+    if (!scratch_for(dev, (size_t)T * rows * N, (size_t)N / 64 + 1, &part, &counters)) return -1;
+    if (rows == 1 && tf_tma_ok(idx, codebook, K, N, n_codes, tf_config(K, N, n_codes, E_Y)))
+        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, part, counters, y) ? 0 : -1;
     if (!tt_gemv_partials(s, x, rows, codebook, n_codes, idx, K, N, part)) return -1;
     if (!tt_reduce_partials(s, part, T, rows, N, y)) return -1;
     return 0;
