@@ -26,6 +26,7 @@
 // streams and codebooks start before griddepcontrol.wait, so they overlap
 // the previous kernel.  Each step is captured once as a CUDA graph and
 // replayed; the step position and token live in device memory.
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -671,6 +672,17 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     return true;
 }
 
+// Programmatic dependent launch (KLLM_PDL=1).  Off by default: measured on
+// B200, the early-resident dependent CTAs slowed a decode step from 1.56 ms
+// to 2.45 ms (graph replay, TinyLlama-architecture chip).
+bool pdl_enabled() {
+    static int on = [] {
+        const char *v = getenv("KLLM_PDL");
+        return v && *v == '1' ? 1 : 0;
+    }();
+    return on != 0;
+}
+
 template <class Kern, class... Args>
 static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t smem,
                        Args... args) {
@@ -683,7 +695,7 @@ static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t 
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     g_launches++;
     return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
 }
@@ -732,7 +744,7 @@ static bool record_step(CtxImpl *c, DecodePlan *p) {
         a.gen_host = (volatile int *)p->gen_host_dev;
         a.max_gen = p->max_pos;
         a.status = p->status;
-        return launch_tt_fused(s, p->cfgs[mi], p->maps[mi], a, true);
+        return launch_tt_fused(s, p->cfgs[mi], p->maps[mi], a, pdl_enabled());
     };
     for (int l = 0; l < t.L; l++) {
         const LayerSlots &ls = t.layers[l];

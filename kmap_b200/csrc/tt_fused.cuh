@@ -215,7 +215,9 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
             xs[r] = __fmul_rn(__fmul_rn(h[k0 + r], rsq), a.norm_w[k0 + r]);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-    if (!mbar_wait(cbar, 0, a.status)) return;
+    // a wait that gives up (status flagged) skips the math but still passes
+    // every barrier below, so no warp is left waiting at one
+    bool ok = mbar_wait(cbar, 0, a.status);
 
     // -------------------------------------------------------------- core --
     constexpr int WPS = NCW / NSUB;                 // warps per sub-box
@@ -225,9 +227,12 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
 #pragma unroll
     for (int c = 0; c < CPL; c++) acc[c] = 0.0f;
 
-    for (int b = 0; b < nbox; b++) {
+    for (int b = 0; ok && b < nbox; b++) {
         const int s = b % NS;
-        if (!mbar_wait(&full[s], (b / NS) & 1, a.status)) return;
+        if (!mbar_wait(&full[s], (b / NS) & 1, a.status)) {
+            ok = false;
+            break;
+        }
         const uint16_t *tile = stage + (size_t)s * BR * BN + q * BR * BW + wcol;
         const float *xb = xs + b * BR;
         const int rows = min(BR, len - b * BR);
@@ -273,7 +278,7 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
     asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
     if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[jb], 1) == T - 1;
     asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-    if (!s_last) return;
+    if (!s_last) return;   // uniform across the CTA
     __threadfence();
     // the last CTA of this column block: ordered sum of the T partials
     const float *P = a.part;

@@ -120,7 +120,18 @@ TFConfig tf_config(int K, int N, int n_codes, int emode) {
     c.nsub = emode == E_SWIGLU ? 2 : 1;
     long long cols = emode == E_SWIGLU ? N / 2 : N;
     c.cpl = cols >= 8192 ? 2 : 1;
-    c.stages = 2;
+    // Ring depth: a grid that fits in one wave keeps its whole chunk in
+    // flight (one DRAM round trip); larger grids leave room for more CTAs
+    // per SM instead.
+    const int T = tt_chunks(K);
+    const long long ctas = (long long)((cols + c.bw() - 1) / c.bw()) * T;
+    const int nbox = ((K + T - 1) / T + 31) / 32;
+    const int per_sm = (int)std::max<long long>(1, (ctas + 147) / 148);
+    const size_t fixed = (size_t)n_codes * 4 + 4096;
+    const size_t budget = per_sm <= 1 ? 200 * 1024 : (size_t)(220 * 1024) / per_sm;
+    const size_t stage_bytes = (size_t)c.bn() * 32 * 2;
+    int st = budget > fixed ? (int)((budget - fixed) / stage_bytes) : 2;
+    c.stages = std::max(2, std::min(std::min(st, nbox), 12));
     int e = env_int("KLLM_TT_CPL", 0);
     if (e == 1 || e == 2 || e == 4) c.cpl = e;
     e = env_int("KLLM_TT_STAGES", 0);
