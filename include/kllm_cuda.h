@@ -111,6 +111,20 @@ int kllm_tt_gemv(const float *x, int rows, const float *codebook, int n_codes,
 int kllm_tt_gemv_host(const float *x, int rows, const float *codebook,
                       int n_codes, const uint16_t *idx, int K, int N, float *y);
 
+/* Allocation-free form of kllm_tt_gemv for one row (x is [K], y is [N]).
+ * No counterpart in the reference runtime.  For callers that may not
+ * allocate device memory -- code running during CUDA graph capture, plugins
+ * whose host framework owns the device memory pool, fixed-footprint
+ * real-time hosts -- it keeps its scratch in a fixed array inside the
+ * library's device image instead of growing one with cudaMalloc: N is at
+ * most 65536 (2 MiB of partial rows per device, held until exit); larger N
+ * is rejected with an error.  The first call on a device looks up the
+ * array's device address and should come before any stream capture.  Calls
+ * whose kernels overlap on the GPU share the array and race.  Same result,
+ * bit for bit, as kllm_tt_gemv; every index must be < n_codes. */
+int kllm_tt_gemv_noalloc(const float *x, const float *codebook, int n_codes,
+                         const uint16_t *idx, int K, int N, float *y, void *stream);
+
 /* ------------------------------------------------------------- chips -----
  * Chip directory loader: the same files, read the same way, as the
  * reference CLI's static chip_load (csrc/kllm.c:152-388): processor.json,

@@ -133,7 +133,7 @@ TFConfig tf_config(int K, int N, int n_codes, int emode) {
     int st = budget > fixed ? (int)((budget - fixed) / stage_bytes) : 2;
     c.stages = std::max(2, std::min(std::min(st, nbox), 12));
     int e = env_int("KLLM_TT_CPL", 0);
-    if (e == 1 || e == 2 || e == 4) c.cpl = e;
+    if (e == 1 || e == 2) c.cpl = e;
     e = env_int("KLLM_TT_STAGES", 0);
     if (e >= 1 && e <= 16) c.stages = e;
     return c;
@@ -146,7 +146,7 @@ int tf_blocks(const TFConfig &c, int N, int F, int emode) {
 bool tf_tma_ok(const uint16_t *idx, const float *cb, int K, int N, int n_codes,
                const TFConfig &c) {
     return K > 0 && N >= 8 && (N % 8) == 0 && ((uintptr_t)idx % 16) == 0 &&
-           ((uintptr_t)cb % 16) == 0 && n_codes <= 16384 && c.bw() % 8 == 0;
+           ((uintptr_t)cb % 16) == 0 && n_codes <= 16384 && c.bw() % 8 == 0 && c.bw() <= 256;
 }
 
 template <int NCW, int CPL, int NSUB>
