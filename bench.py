@@ -164,6 +164,26 @@ def ttgemv_roofline(device_index):
     return res
 
 
+def ttgemv_once(K, N, C, reps):
+    """kllm_tt_gemv on one seeded config-1 shape, `reps` launches (for ncu)."""
+    import torch
+
+    import kmap_b200
+    lib = kmap_b200.lib()
+    x, cb, idx = chipgen.tt_case(7, K, N, C)
+    dev = torch.device("cuda", 0)
+    di = torch.from_numpy(idx.view(np.int16)).to(dev)
+    dc = torch.from_numpy(np.pad(cb, (0, (-len(cb)) % 4))).to(dev)
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty(N, device=dev)
+    for _ in range(reps):
+        rc = lib.kllm_tt_gemv(dx.data_ptr(), 1, dc.data_ptr(), C, di.data_ptr(), K, N,
+                              dy.data_ptr(), None)
+        assert rc == 0, kmap_b200.last_error()
+    torch.cuda.synchronize()
+    log("ttgemv %dx%d ok" % (K, N))
+
+
 # ---------------------------------------------------------------- arms ---
 
 def reference_sample(chip, n_prompt=4, n_gen=4, threads=None):
@@ -322,7 +342,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ttgemv-shape", type=int, nargs=3, metavar=("K", "N", "CODES"),
+                    help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
+                         "--steps times and exit (no JSON line)")
     args = ap.parse_args()
+    if args.ttgemv_shape:
+        ttgemv_once(*args.ttgemv_shape, reps=args.steps)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

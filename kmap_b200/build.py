@@ -55,6 +55,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         changed = True
     if changed or force or not os.path.exists(LIB):
         _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-Xlinker", "-Bsymbolic",
+              "-Xlinker", "-soname=libkllm_cuda.so",
               "-lpthread", "-ldl", "-lrt"])
     return LIB
 
