@@ -37,6 +37,7 @@
 #include "plan.cuh"
 #include "sm100.cuh"
 #include "tt_fused.cuh"
+#include "persist.cuh"
 
 namespace kllm {
 
@@ -485,6 +486,19 @@ struct DecodePlan {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     float *graph_hist = nullptr;   // history buffer baked into the graph
+    // persistent step kernel
+    bool persist = false;
+    int mk_grid = 0, mk_stages = 0;
+    size_t mk_smem = 0;
+    MKArgs mk = {};
+    std::vector<MKPhase> phases;
+    MKPhase *d_phases = nullptr;
+    CUtensorMap *d_maps = nullptr;
+    const float **d_cbp = nullptr;
+    int *d_ncodes = nullptr;
+    int *d_done = nullptr, *d_abort = nullptr;
+    float *hbuf = nullptr;            // [2][H] residual versions
+    float *pq = nullptr, *po = nullptr, *pg = nullptr, *pd = nullptr, *pl = nullptr;
     long long kernels_per_step = 0;
     int graph_hist_rows = 0;
     int logits_slot = -1;
@@ -502,6 +516,10 @@ static void free_plan(DecodePlan *p) {
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (float *b : p->dev_norm)
+        if (b) cudaFree(b);
+    void *mbufs[] = {p->d_phases, p->d_maps, p->d_cbp, p->d_ncodes, p->d_done, p->d_abort,
+                     p->hbuf, p->pq, p->po, p->pg, p->pd, p->pl};
+    for (void *b : mbufs)
         if (b) cudaFree(b);
     if (p->gen_host) cudaFreeHost(p->gen_host);
     for (cudaEvent_t e : {p->ev0, p->ev1, p->ev2})
@@ -522,6 +540,183 @@ void plan_destroy(CtxImpl *c) {
 template <class T>
 static bool dalloc(T **p, size_t n) {
     return KLLM_CUDA(cudaMalloc((void **)p, std::max<size_t>(n, 1) * sizeof(T)));
+}
+
+// Persistent step kernel: phase list, tensor maps with each phase's box,
+// scratch, shared-memory layout and co-residency check.  Returns false (no
+// error recorded) when the kernel cannot be used; the per-kernel plan stays.
+static bool env_on(const char *name, bool dflt) {
+    const char *v = getenv(name);
+    if (!v || !*v) return dflt;
+    return *v != '0';
+}
+
+static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &tts) {
+    if (!env_on("KLLM_PERSIST", true)) return false;
+    const TapeCtx *ctx = &c->base;
+    const TemplateInfo &t = p->ti;
+    const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, nq = qd + 2 * nkv * hd;
+    const int F = t.F, V = t.V, L = t.L;
+    const int nmat = (int)tts.size();
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
+    // geometry per matrix role: cpl / nsub
+    auto role_of = [&](int i) { return i + 1 == nmat ? 4 : i % 4; };   // 0 qkv 1 o 2 gu 3 dn 4 lm
+    auto cpl_of = [](int r) { return (r == 2 || r == 4) ? 2 : 1; };
+    auto nsub_of = [](int r) { return r == 2 ? 2 : 1; };
+    // tensor maps (box per role)
+    std::vector<CUtensorMap> maps(nmat);
+    std::vector<const float *> cbp(nmat);
+    std::vector<int> ncodes(nmat);
+    int cb_cap = 4;
+    for (int i = 0; i < nmat; i++) {
+        const Slot &sl = ctx->slots[tts[i]];
+        const DevSlot &w = c->ds[tts[i]];
+        const int r = role_of(i), cpl = cpl_of(r), nsub = nsub_of(r);
+        const int bw = 128 * cpl / nsub, br = mk_box_rows(cpl, nsub);
+        if (sl.tt_N % 8 || ((uintptr_t)w.d_idx % 16) || ((uintptr_t)w.d_cb % 16)) return false;
+        if (!make_idx_tmap(&maps[i], w.d_idx, sl.tt_K, sl.tt_N, bw, br)) return false;
+        cbp[i] = w.d_cb;
+        ncodes[i] = sl.n_codes;
+        cb_cap = std::max(cb_cap, (sl.n_codes + 3) & ~3);
+    }
+    const int T_h = tt_chunks(H), T_qd = tt_chunks(qd), T_f = tt_chunks(F);
+    const int max_len = std::max({(H + T_h - 1) / T_h, (qd + T_qd - 1) / T_qd, (F + T_f - 1) / T_f});
+    const int h_cap = (H + 3) & ~3, xs_cap = (max_len + 3) & ~3, sc_cap = (p->max_pos + 3) & ~3;
+    const size_t fixed = (size_t)4 * (2 * cb_cap + h_cap + xs_cap + sc_cap) + 64;
+    const size_t budget = 220 * 1024;
+    if (fixed + 2 * (MK_STAGE + 16) > budget) return false;
+    const int S = (int)std::min<size_t>(24, (budget - fixed) / (MK_STAGE + 16));
+    const size_t smem = (size_t)S * (MK_STAGE + 16) + fixed;
+    auto kern = hd == 32 ? k_decode_step<32> : hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem)))
+        return false;
+    int per_sm = 0;
+    if (!KLLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, MK_THREADS, smem)) ||
+        per_sm < 1)
+        return false;
+    // scratch
+    auto fa = [&](float **b, size_t n) { return dalloc(b, n); };
+    if (!fa(&p->hbuf, 2 * (size_t)H) || !fa(&p->pq, (size_t)T_h * nq) ||
+        !fa(&p->po, (size_t)T_qd * H) || !fa(&p->pg, (size_t)T_h * 2 * F) ||
+        !fa(&p->pd, (size_t)T_f * H) || !fa(&p->pl, (size_t)T_h * V))
+        return false;
+    // phases
+    std::vector<MKPhase> ph;
+    auto gemv = [&](int mi, int K, int N, int xmode, const float *x, const float *xpart,
+                    int xT, int xN, const float *nw, float eps, float *hout, float *part) {
+        MKPhase m = {};
+        const int r = role_of(mi), cpl = cpl_of(r), nsub = nsub_of(r);
+        m.kind = PH_GEMV;
+        m.mat = mi;
+        m.K = K;
+        m.N = N;
+        m.T = tt_chunks(K);
+        m.cpl = cpl;
+        m.nsub = nsub;
+        m.F = F;
+        m.ncb = nsub == 2 ? (F + 127) / 128 : (N + 128 * cpl - 1) / (128 * cpl);
+        m.ntasks = m.ncb * m.T;
+        m.xmode = xmode;
+        m.x = x;
+        m.xpart = xpart;
+        m.xpart_T = xT;
+        m.xpart_N = xN;
+        m.norm_w = nw;
+        m.eps = eps;
+        m.h_out = hout;
+        m.part = part;
+        ph.push_back(m);
+    };
+    float *hb[2] = {p->hbuf, p->hbuf + H};
+    for (int l = 0; l < L; l++) {
+        if (l == 0)
+            gemv(4 * l, H, nq, PX_NORM_EMBED, nullptr, nullptr, 0, 0, p->dev_norm[2 * l],
+                 p->eps[2 * l], hb[0], p->pq);
+        else
+            gemv(4 * l, H, nq, PX_NORM_RES, hb[1], p->pd, T_f, H, p->dev_norm[2 * l],
+                 p->eps[2 * l], hb[0], p->pq);
+        MKPhase at = {};
+        at.kind = PH_ATT;
+        at.ntasks = t.nh;
+        at.layer = l;
+        ph.push_back(at);
+        gemv(4 * l + 1, qd, H, PX_VEC, p->ctx, nullptr, 0, 0, nullptr, 0.f, nullptr, p->po);
+        gemv(4 * l + 2, H, 2 * F, PX_NORM_RES, hb[0], p->po, T_qd, H, p->dev_norm[2 * l + 1],
+             p->eps[2 * l + 1], hb[1], p->pg);
+        gemv(4 * l + 3, F, H, PX_SWIGLU, nullptr, p->pg, T_h, 2 * F, nullptr, 0.f, nullptr, p->pd);
+    }
+    gemv(nmat - 1, H, V, PX_NORM_RES, hb[1], p->pd, T_f, H, p->dev_norm.back(), p->f_eps, hb[0],
+         p->pl);
+    MKPhase am = {};
+    am.kind = PH_ARGMAX;
+    am.ntasks = std::min(sms, 1024);
+    ph.push_back(am);
+    // device copies
+    if (!KLLM_CUDA(cudaMalloc((void **)&p->d_phases, ph.size() * sizeof(MKPhase))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_phases, ph.data(), ph.size() * sizeof(MKPhase),
+                              cudaMemcpyHostToDevice)) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_maps, nmat * sizeof(CUtensorMap))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_maps, maps.data(), nmat * sizeof(CUtensorMap),
+                              cudaMemcpyHostToDevice)) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_cbp, nmat * sizeof(float *))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_cbp, cbp.data(), nmat * sizeof(float *),
+                              cudaMemcpyHostToDevice)) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_ncodes, nmat * sizeof(int))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_ncodes, ncodes.data(), nmat * sizeof(int),
+                              cudaMemcpyHostToDevice)) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_done, (ph.size() + 1) * sizeof(int))) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_abort, sizeof(int))) ||
+        !KLLM_CUDA(cudaMemset(p->d_abort, 0, sizeof(int))))
+        return false;
+    if (((uintptr_t)p->d_maps % 64) != 0) return false;
+    p->phases = ph;
+    MKArgs &a = p->mk;
+    a.phases = p->d_phases;
+    a.nphases = (int)ph.size();
+    a.maps = p->d_maps;
+    a.cbp = p->d_cbp;
+    a.ncodes = p->d_ncodes;
+    a.done = p->d_done;
+    a.status = p->status;
+    a.abort = p->d_abort;
+    a.stages = S;
+    a.cb_cap = cb_cap;
+    a.h_cap = h_cap;
+    a.xs_cap = xs_cap;
+    a.sc_cap = sc_cap;
+    a.H = H;
+    a.st = p->st;
+    a.embed = p->embed;
+    a.prompt = p->prompt;
+    a.gen = p->gen;
+    a.gen_host = (volatile int *)p->gen_host_dev;
+    a.vocab = V;
+    a.max_gen = p->max_pos;
+    a.qkv_part = p->pq;
+    a.qkv_T = T_h;
+    a.nq = nq;
+    a.nh = t.nh;
+    a.nkv = nkv;
+    a.groups = t.groups;
+    a.max_pos = p->max_pos;
+    a.rope_cos = p->rcos;
+    a.rope_sin = p->rsin;
+    a.kc = p->kc;
+    a.vc = p->vc;
+    a.scale = p->scale;
+    a.ctx = p->ctx;
+    a.lm_part = p->pl;
+    a.lm_T = T_h;
+    a.logits = p->logits;
+    a.cand_v = p->cand_v;
+    a.cand_i = p->cand_i;
+    p->mk_grid = sms;
+    p->mk_stages = S;
+    p->mk_smem = smem;
+    p->persist = true;
+    return true;
 }
 
 bool plan_match(const TapeCtx *ctx, const PlanDesc &d, std::string *why) {
@@ -668,6 +863,10 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     if (!KLLM_CUDA(cudaEventCreate(&p->ev0)) || !KLLM_CUDA(cudaEventCreate(&p->ev1)) ||
         !KLLM_CUDA(cudaEventCreate(&p->ev2)))
         return fail();
+    if (!persist_prepare(c, p, tts)) {
+        kllm_clear_error();   // the per-kernel plan remains available
+        p->persist = false;
+    }
     c->plan = p;
     return true;
 }
@@ -700,8 +899,34 @@ static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t 
     return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
 }
 
+// One tape step as a single cooperative launch (arrival counters cleared
+// first).
+static bool record_step_persist(CtxImpl *c, DecodePlan *p) {
+    MKArgs a = p->mk;
+    a.hist = p->hist;
+    a.hist_rows = p->hist_rows;
+    if (!KLLM_CUDA(cudaMemsetAsync(p->d_done, 0, (p->phases.size() + 1) * sizeof(int),
+                                   c->stream)))
+        return false;
+    auto kern = p->ti.hd == 32 ? k_decode_step<32>
+                               : p->ti.hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p->mk_grid);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = p->mk_smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    g_launches++;
+    return KLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
 // All kernels of one tape step, in stream order.
 static bool record_step(CtxImpl *c, DecodePlan *p) {
+    if (p->persist) return record_step_persist(c, p);
     cudaStream_t s = c->stream;
     const TemplateInfo &t = p->ti;
     const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, nq = qd + 2 * nkv * hd;
@@ -834,6 +1059,7 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
                                    cudaMemcpyHostToDevice, s)) ||
         !KLLM_CUDA(cudaMemcpyAsync(p->st, &st0, sizeof st0, cudaMemcpyHostToDevice, s)) ||
         !KLLM_CUDA(cudaMemsetAsync(p->status, 0, 4, s)) ||
+        (p->d_abort && !KLLM_CUDA(cudaMemsetAsync(p->d_abort, 0, 4, s))) ||
         !KLLM_CUDA(cudaStreamSynchronize(s)))
         return false;
     for (int i = 0; i < max_pos; i++) p->gen_host[i] = -1;
