@@ -59,9 +59,11 @@ def peaks():
         return {}
 
 
-def config0_chip(rank=0):
+def config0_chip(rank=0, layers=None):
     spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
     spec.max_seq = 2048
+    if layers:
+        spec.num_layers = layers
     lock = os.path.join(CHIP_CACHE, ".lock")
     os.makedirs(CHIP_CACHE, exist_ok=True)
     import fcntl
@@ -200,6 +202,24 @@ def reference_sample(chip, n_prompt=4, n_gen=4, threads=None):
     dt = time.perf_counter() - t
     ref.L.refh_chip_destroy(h)
     return {"value": (n_prompt + len(toks)) / dt, "seconds": dt, "tokens": n_prompt + len(toks)}
+
+
+def decode_small(layers, steps, warmup):
+    """Decode PROMPT + 16 tokens on a reduced-depth TinyLlama-width chip."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    chip = kmap_b200.Chip(config0_chip(0, layers))
+    p = prompt_ids()
+    for _ in range(max(warmup, 1)):
+        chip.infer(p, 16)
+    ms, n = 0.0, 0
+    for _ in range(steps):
+        toks = chip.infer(p, 16)
+        st = chip.stats()
+        ms += st["prefill_ms"] + st["decode_ms"]
+        n += PROMPT + len(toks)
+    log("%d layers: %.1f us per tape step (fused=%d)" % (layers, 1e3 * ms / n, chip.stats()["fused"]))
+    chip.close()
 
 
 def run_reference_arm(args, rank, world):
@@ -342,12 +362,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling aid: decode on a TinyLlama-width chip with this many "
+                         "layers (small enough for a profiler), print ms per tape step, "
+                         "exit (no JSON line)")
     ap.add_argument("--ttgemv-shape", type=int, nargs=3, metavar=("K", "N", "CODES"),
                     help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
                          "--steps times and exit (no JSON line)")
     args = ap.parse_args()
     if args.ttgemv_shape:
         ttgemv_once(*args.ttgemv_shape, reps=args.steps)
+        return
+    if args.layers:
+        decode_small(args.layers, args.steps, args.warmup)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

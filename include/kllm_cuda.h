@@ -128,7 +128,7 @@ int kllm_tt_gemv_noalloc(const float *x, const float *codebook, int n_codes,
 /* ------------------------------------------------------------- chips -----
  * Chip directory loader: the same files, read the same way, as the
  * reference CLI's static chip_load (csrc/kllm.c:152-388): processor.json,
- * tables/*.bin, bpe/*, circuit/tape.bin + slots.bin + const_<slot>*.bin.
+ * tables/<name>.bin, bpe/<files>, circuit/tape.bin + slots.bin + const_<slot>*.bin.
  * The loader validates what the reference trusts (file sizes against
  * slots.bin, the 276-byte record size, slot ids in processor.json) and
  * returns NULL with kllm_last_error() set instead of exiting. */

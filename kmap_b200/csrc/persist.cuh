@@ -1,104 +1,106 @@
 // persist.cuh -- the persistent decode step: one cooperative launch runs a
 // whole tape step of the compiler's LLaMA template.
 //
-// Grid = one CTA per SM (all co-resident: cooperative launch).  Each CTA has
-// one producer warp and four consumer warps.  The step is a list of phases
-// (per layer: QKV, attention, O, gate_up, down; then lm_head and argmax).
-// Tasks of a phase are dealt round-robin to the CTAs.
+// Grid = one CTA per SM (co-resident: cooperative launch).  Each CTA has one
+// producer warp and four consumer warps.  The step is a list of phases; per
+// layer QKV, attention, O, gate_up, down; then lm_head.  A GEMV task is one
+// column group (8 columns x all chunks, ttx.cuh) for one warp; task i of a
+// phase goes to CTA i mod G, and a CTA deals its tasks to its warps in turn.
 //
-// Producer: walks the CTA's GEMV tiles of every phase in order and streams
-// their index boxes (16 KB each) through a ring of shared-memory stages with
-// 2-D TMA tile loads (no multicast), loading each matrix's codebook into one
-// of two shared-memory slots ahead of its tiles.  Weights do not depend on
-// activations, so the stream runs ahead across phase boundaries, limited
-// only by ring space.
+// Producer warp: lane 0 streams the CTA's tasks' slot streams through a ring
+// of 16 KB stages with bulk copies, in the order the warps consume them
+// (rounds of up to four tasks, piece by piece).  Weights do not depend on
+// activations, so the stream runs ahead across phase boundaries.  Lane 1
+// loads each phase's codebook (copy 0 of the table) and norm weights once
+// the consumers released the previous ones.
 //
-// Consumers: for each phase, wait until every CTA has finished the previous
-// one (a device-wide arrival counter, polled with a time limit), then do the
-// CTA's tasks:
-//   GEMV      x for the tile's chunk (plain vector, rmsnorm of the residual,
-//             or silu(gate) * up from the gate_up partials), then the chunk's
-//             rows in order -- acc = fl(acc + fl(x * cb[idx])), the
-//             reference's serial chunk sum -- and the partial row to HBM
-//   attention one head: ordered chunk sums of the QKV partials, RoPE, KV
-//             append, softmax(q.K^T * scale).V
-//   argmax    a slice of the vocabulary: logits = ordered chunk sums of the
-//             lm_head partials, first maximum; the CTA that finishes last
-//             picks the token and advances the step.
-// Chunk partials are always added in chunk order (_tape_runner.c:646-662),
-// so every TT-GEMV result is bit-identical to the reference's.
+// Consumers, per phase: build the codebook copies 1..R-1 in shared memory;
+// wait until every CTA finished the phase this one reads (a device-wide
+// counter, polled with a time limit); stage x in shared memory, chunk by
+// chunk (rmsnorm of the residual, the embedding row in layer 0, or a plain
+// vector: ctx, act).  GEMV task, lane = 8 * pair + chunk:
+//   rows   acc = fl(acc + fl(x[k] * cb[idx[k][n]])) over the chunk's rows in
+//          order -- the reference's serial chunk sum (_tape_runner.c:530-545);
+//   sum    chunk sums added in chunk order through shuffles
+//          (_tape_runner.c:646-662): every TT-GEMV result is bit-identical
+//          to the reference's;
+//   out    RoPE + KV append (QKV), residual add (O, down), silu(gate) * up
+//          (gate_up), logits + first maximum (lm_head; the CTA that finishes
+//          last picks the token).
+// Attention: one head per task; q and the cache are final by then.
 //
-// Residual versions alternate between two HBM buffers: the phase that needs
-// rmsnorm(h) rebuilds h = h_prev + sum_t part[t] in every CTA (shared
-// memory) and CTA 0 stores it for later phases.
+// Every wait is bounded; a wait that gives up raises the abort flag, and
+// the consumers of every CTA leave at the next phase boundary together
+// (named barriers are never split).
 #pragma once
 
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tt_fused.cuh"
+#include "ttx.cuh"
 
 namespace kllm {
 
-enum PhaseKind : int { PH_GEMV = 0, PH_ATT = 1, PH_ARGMAX = 2 };
-enum PhaseX : int { PX_VEC = 0, PX_NORM_EMBED = 1, PX_NORM_RES = 2, PX_SWIGLU = 3 };
+enum DSKind : int { DS_GEMV = 0, DS_ATT = 1 };
+enum DSX : int { DX_EMBED = 0, DX_NORM = 1, DX_VEC = 2 };
+enum DSE : int { DE_QKV = 0, DE_RESID = 1, DE_SWIGLU = 2, DE_LM = 3 };
 
-struct MKPhase {
-    int kind, ntasks;
-    // GEMV
-    int mat, K, N, T, ncb, cpl, nsub, F, xmode;
-    const float *x;        // PX_VEC: input; PX_NORM_RES: previous residual version
-    const float *xpart;    // PX_NORM_RES / PX_SWIGLU: partial rows to reduce
-    int xpart_T, xpart_N;
+struct DSPhase {
+    int kind, ntasks;          // GEMV: column groups; attention: heads
+    int dep, dep_count;        // wait for done[dep] >= dep_count (dep < 0: none)
+    TTXDesc d;                 // GEMV layout (ttx.cuh)
+    int npieces;               // 16-step pieces per group
+    int xs;                    // floats per chunk row of the staged x
+    const uint8_t *stream;
+    const float *cb;           // raw codebook (copy 0 of the table)
+    int cb_bytes;              // n_codes * 4 rounded up to 16
+    int xmode, emode;
+    const float *x;            // DX_NORM: residual; DX_VEC: input vector
     const float *norm_w;
     float eps;
-    float *h_out;          // norm phases: CTA 0 stores the new residual version
-    float *part;           // output partial rows [T][N]
-    // attention
+    const float *hold;         // DE_RESID: residual in (nullptr: embedding row)
+    float *out;                // q / new residual / act / logits
     int layer;
 };
 
-struct MKArgs {
-    const MKPhase *phases;
+struct DSArgs {
+    const DSPhase *phases;
     int nphases;
-    const CUtensorMap *maps;     // per matrix
-    const float *const *cbp;     // per matrix (padded to a multiple of 4 floats)
-    const int *ncodes;           // per matrix
-    int *done;                   // per phase arrival counters (zeroed per step)
+    int *done;                 // [nphases] arrivals (zeroed per step)
     int *status;
     int *abort;
-    int stages, cb_cap, h_cap, xs_cap, sc_cap;
-    int H;
+    int stages, tab_cap, xc_cap;
     // step state and embedding
     StepState *st;
     const float *embed;
     const int *prompt;
     int *gen;
     volatile int *gen_host;
-    int vocab, max_gen;
+    int vocab, max_gen, H;
     // attention
-    const float *qkv_part;
-    int qkv_T, nq, nh, nkv, groups, max_pos;
+    float *q;
+    int nh, nkv, groups, max_pos, qd, kvd;
     const float *rope_cos, *rope_sin;
-    float *kc, *vc;              // [L][nkv][max_pos][hd]
+    float *kc, *vc;            // [L][nkv][max_pos][hd]
     float scale;
     float *ctx;
-    // argmax
-    const float *lm_part;
-    int lm_T;
-    float *logits, *hist;
+    // lm_head
+    float *hist;
     int hist_rows;
-    float *cand_v;
+    float *cand_v;             // [G] per-CTA first maxima
     int *cand_i;
 };
 
-constexpr int MK_NCW = 4;
-constexpr int MK_NC = MK_NCW * 32;
-constexpr int MK_THREADS = (MK_NCW + 1) * 32;
-constexpr int MK_STAGE = 16384;   // bytes per ring stage (one box, or two half boxes)
-
-__host__ __device__ inline int mk_box_rows(int cpl, int nsub) {
-    return (cpl == 1 && nsub == 1) ? 64 : 32;   // 128 x 64 or 256 x 32 uint16
-}
+constexpr int DS_NCW = 8;                    // consumer warps
+constexpr int DS_NC = DS_NCW * 32;
+constexpr int DS_PRODUCER = DS_NCW;          // warp: streams the ring
+constexpr int DS_TABLER = DS_NCW + 1;        // warp: builds codebook tables
+constexpr int DS_THREADS = (DS_NCW + 2) * 32;
+constexpr int DS_MAX_STAGES = 32;
+constexpr int DS_PIECE_STEPS = 16;           // steps per ring stage (16 KB: one issuing
+                                             // thread keeps HBM busy only with pieces this big)
+constexpr int DS_STAGE = DS_PIECE_STEPS * TTX_STEP;
+constexpr int DS_XU = 24;                    // x values per consumer thread in flight
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
@@ -106,8 +108,8 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
     return v;
 }
 
-// Wait until *ctr >= target; false (abort raised) on timeout or abort.
-__device__ __forceinline__ bool mk_wait_counter(const int *ctr, int target, int *status,
+// Wait until *ctr >= target; false on abort or timeout (which raises abort).
+__device__ __forceinline__ bool ds_wait_counter(const int *ctr, int target, int *status,
                                                 int *abort) {
     if (ld_acquire(ctr) >= target) return true;
     const unsigned long long t0 = globaltimer();
@@ -118,109 +120,257 @@ __device__ __forceinline__ bool mk_wait_counter(const int *ctr, int target, int 
             atomicExch(abort, 1);
             return false;
         }
-        __nanosleep(64);
+        __nanosleep(20);
     }
     return true;
 }
 
-__device__ __forceinline__ void cbar_sync() {
-    asm volatile("bar.sync 1, %0;" ::"r"(MK_NC) : "memory");
+// Wait until the stage tag says the stage holds piece `seq`.
+__device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *status) {
+    if (*tag == seq) return true;
+    const unsigned long long t0 = globaltimer();
+    while (*tag != seq) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicOr(status, ST_WAIT_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
 }
 
-// Fixed-shape sum over the consumer threads (same result in every CTA).
-__device__ __forceinline__ float mk_block_sum(float v, float *red) {
+__device__ __forceinline__ void cbar_sync() {   // the consumer warps
+    asm volatile("bar.sync 1, %0;" ::"n"(DS_NC) : "memory");
+}
+
+// Fixed-shape sum over the consumer threads: the same bits in every CTA.
+__device__ __forceinline__ float ds_block_sum(float v, float *red) {
     for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    cbar_sync();   // red[] may still be read from its previous use
     if (l == 0) red[w] = v;
     cbar_sync();
-    float r = 0.f;
-    if (w == 0) {
-        r = l < MK_NCW ? red[l] : 0.f;
-        for (int o = 16; o; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
-        if (l == 0) red[MK_NCW] = r;
+    float r = red[0];
+    for (int i = 1; i < DS_NCW; i++) r = __fadd_rn(r, red[i]);
+    return r;
+}
+
+// Token fed at the current position (-1: outside the vocabulary).
+__device__ __forceinline__ int ds_token(const DSArgs &a) {
+    const int pos = a.st->pos, P = a.st->prompt_len;
+    const int tok = pos < P ? a.prompt[pos] : __ldcg(a.gen + pos - P);
+    return (tok < 0 || tok >= a.vocab) ? -1 : tok;
+}
+
+// Index k of x -> its slot in the staged, chunk-major x, for increasing k.
+struct DSSlot {
+    const TTXDesc &d;
+    int xs, t, start, end;
+    __device__ DSSlot(const TTXDesc &dd, int xss) : d(dd), xs(xss), t(0), start(0), end(dd.chunk_len(0)) {}
+    __device__ __forceinline__ int at(int k) {
+        while (k >= end && t + 1 < d.T) {
+            t++;
+            start = end;
+            end += d.chunk_len(t);
+        }
+        return t * xs + (k - start);
     }
-    cbar_sync();
-    return red[MK_NCW];
+};
+
+__device__ __forceinline__ uint32_t lo16(uint32_t w) { return w & 0xffffu; }
+__device__ __forceinline__ uint32_t hi16(uint32_t w) { return w >> 16; }
+
+// Slot -> table word for the two halves of a stream word.
+__device__ __forceinline__ float2 ds_gather(const float *tab, uint32_t w0, uint32_t w1, int hi) {
+    return hi ? make_float2(tab[hi16(w0)], tab[hi16(w1)])
+              : make_float2(tab[lo16(w0)], tab[lo16(w1)]);
+}
+
+// The 8 gathered (column 0, column 1) pairs of one step.
+struct DSVals {
+    float2 v[8];
+};
+
+__device__ __forceinline__ DSVals ds_gather_step(const float *tab, const uint4 &q0, const uint4 &q1) {
+    DSVals r;
+    r.v[0] = ds_gather(tab, q0.x, q1.x, 0);
+    r.v[1] = ds_gather(tab, q0.x, q1.x, 1);
+    r.v[2] = ds_gather(tab, q0.y, q1.y, 0);
+    r.v[3] = ds_gather(tab, q0.y, q1.y, 1);
+    r.v[4] = ds_gather(tab, q0.z, q1.z, 0);
+    r.v[5] = ds_gather(tab, q0.z, q1.z, 1);
+    r.v[6] = ds_gather(tab, q0.w, q1.w, 0);
+    r.v[7] = ds_gather(tab, q0.w, q1.w, 1);
+    return r;
+}
+
+__device__ __forceinline__ DSVals ds_load_step(const uint8_t *lp, const float *tab) {
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(lp);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(lp + 512);
+    return ds_gather_step(tab, q0, q1);
+}
+
+__device__ __forceinline__ float2 ds_mac_step(const float *xr, const DSVals &v, float2 acc) {
+    const float4 xa = *reinterpret_cast<const float4 *>(xr);
+    const float4 xb = *reinterpret_cast<const float4 *>(xr + 4);
+    const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    float2 p[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) p[e] = __fmul2_rn(make_float2(xv[e], xv[e]), v.v[e]);
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc = __fadd2_rn(acc, p[e]);
+    return acc;
+}
+
+// Steps [0, n) of a piece whose every row is inside the lane's chunk, in
+// order.  Two register sets of two steps each: the codebook values of the
+// next two steps are in flight while the current two are multiplied and
+// added in row order.
+__device__ __forceinline__ float2 ds_steps_full(const uint8_t *pc, int lane, const float *xr,
+                                                int n, const float *tab, float2 acc) {
+    const uint8_t *lp = pc + lane * 16;
+    int i = 0;
+    if (n >= 4) {
+        DSVals a0 = ds_load_step(lp, tab), a1 = ds_load_step(lp + TTX_STEP, tab);
+        for (; i + 4 <= n; i += 4) {
+            const DSVals b0 = ds_load_step(lp + (i + 2) * TTX_STEP, tab);
+            const DSVals b1 = ds_load_step(lp + (i + 3) * TTX_STEP, tab);
+            acc = ds_mac_step(xr + 8 * i, a0, acc);
+            acc = ds_mac_step(xr + 8 * i + 8, a1, acc);
+            if (i + 6 <= n) {
+                a0 = ds_load_step(lp + (i + 4) * TTX_STEP, tab);
+                a1 = ds_load_step(lp + (i + 5) * TTX_STEP, tab);
+            }
+            acc = ds_mac_step(xr + 8 * i + 16, b0, acc);
+            acc = ds_mac_step(xr + 8 * i + 24, b1, acc);
+        }
+    }
+    for (; i < n; i++) acc = ds_mac_step(xr + 8 * i, ds_load_step(lp + i * TTX_STEP, tab), acc);
+    return acc;
+}
+
+// One step of which only the first `rows` rows (< 8, may be <= 0) are in
+// the lane's chunk.
+__device__ __forceinline__ float2 ds_step_tail(const uint8_t *stp, int lane, const float *xr,
+                                               int rows, const float *tab, float2 acc) {
+    if (rows <= 0) return acc;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(stp + lane * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(stp + 512 + lane * 16);
+    const DSVals v = ds_gather_step(tab, q0, q1);
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < rows) acc = __fadd2_rn(acc, __fmul2_rn(make_float2(xr[e], xr[e]), v.v[e]));
+    return acc;
 }
 
 template <int HD>
-__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_step(const __grid_constant__ MKArgs a) {
+__global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_constant__ DSArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float red[MK_NCW + 2];
-    __shared__ float s_rsq;
-    __shared__ int s_tok, s_last;
-    __shared__ float qv[HD], kv[HD], vv[HD], pctx[MK_NC / HD > 0 ? MK_NC / HD : 1][HD];
-    __shared__ int ri[MK_NCW];
+    constexpr int NQ = HD / 4;                 // float4 per head row
+    constexpr int NPG = DS_NC / NQ;            // position groups in P.V
+    __shared__ float red[DS_NCW + 1];
+    __shared__ __align__(16) float qv[HD];
+    __shared__ __align__(16) float pctx[NPG][HD];
+    __shared__ int s_flag, s_tok;
+    __shared__ int ri[DS_NCW];
 
     const int G = gridDim.x, cta = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.stages;
     uint8_t *ring = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * MK_STAGE);
+    float *tabs = reinterpret_cast<float *>(smem + (size_t)S * DS_STAGE);   // 2 tables
+    float *xc = tabs + 2 * a.tab_cap;  // staged x, chunk-major
+    float *sc = xc;                    // attention scores (no GEMV then)
+    uint64_t *full = reinterpret_cast<uint64_t *>(xc + a.xc_cap);
     uint64_t *empty = full + S;
-    uint64_t *cbf = empty + S;
-    uint64_t *cbe = cbf + 2;
-    float *cbs = reinterpret_cast<float *>(cbe + 2);   // 2 slots x cb_cap
-    float *hs = cbs + 2 * a.cb_cap;
-    float *xs = hs + a.h_cap;
-    float *sc = xs + a.xs_cap;
+    uint64_t *tready = empty + S;      // [2] table built
+    uint64_t *tfree = tready + 2;      // [2] table no longer read
+    uint64_t *rawfull = tfree + 2;     // codebook bulk copy landed
+    // Sequence number of the piece each stage holds or awaits.  A consumer
+    // may run a whole ring ahead of another; full[s]'s parity alone cannot
+    // tell its piece from the stage's previous one, the tag can.
+    volatile int *stage_seq = reinterpret_cast<volatile int *>(rawfull + 1);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], MK_NCW);
+            mbar_init(&empty[s], 1);
+            stage_seq[s] = -1;
         }
-        for (int s = 0; s < 2; s++) {
-            mbar_init(&cbf[s], 1);
-            mbar_init(&cbe[s], MK_NCW);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tready[i], 1);
+            mbar_init(&tfree[i], 1);
         }
+        mbar_init(rawfull, 1);
         mbar_fence_init();
     }
     __syncthreads();
 
     // ================================================================ producer
-    if (warp == MK_NCW) {
-        if (lane != 0) return;
-        int seq = 0, q = 0;
-        for (int p = 0; p < a.nphases; p++) {
-            const MKPhase &ph = a.phases[p];
-            if (ph.kind != PH_GEMV || cta >= ph.ntasks) continue;
-            if (ld_acquire(a.abort)) return;
-            const int slot = q & 1;
-            if (q >= 2 && !mbar_wait(&cbe[slot], ((q >> 1) - 1) & 1, a.status)) {
-                atomicExch(a.abort, 1);
-                return;
+    if (warp == DS_TABLER) {
+        {
+            // The tables, two phases deep: the codebook by bulk copy into
+            // copy 0, copies 1..R-1 by the warp's lanes.
+            int q = 0;
+            for (int p = 0; p < a.nphases; p++) {
+                const DSPhase &ph = a.phases[p];
+                if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
+                if (ld_acquire(a.abort)) return;
+                const int slot = q & 1;
+                float *tab = tabs + slot * a.tab_cap;
+                if (q >= 2 && !mbar_wait(&tfree[slot], ((q >> 1) - 1) & 1, a.status)) {
+                    atomicExch(a.abort, 1);
+                    return;
+                }
+                if (lane == 0) {
+                    const uint32_t cb = (uint32_t)ph.cb_bytes;
+                    mbar_expect_tx(rawfull, cb);
+                    for (uint32_t off = 0; off < cb; off += 32768)
+                        bulk_load(reinterpret_cast<uint8_t *>(tab) + off,
+                                  reinterpret_cast<const uint8_t *>(ph.cb) + off,
+                                  min(32768u, cb - off), rawfull);
+                }
+                if (!mbar_wait(rawfull, q & 1, a.status)) {
+                    atomicExch(a.abort, 1);
+                    return;
+                }
+                const int npad = ph.d.npad, R = ph.d.R;
+                for (int e = lane; e < npad; e += 32) {
+                    const float v = tab[e];
+                    for (int c = 1; c < R; c++) tab[c * npad + ttx_swz(e, c)] = v;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tready[slot]);
+                q++;
             }
-            const uint32_t cbytes = (uint32_t)(((a.ncodes[ph.mat] + 3) & ~3) * 4);
-            mbar_expect_tx(&cbf[slot], cbytes);
-            float *dst = cbs + (size_t)slot * a.cb_cap;
-            for (uint32_t off = 0; off < cbytes; off += 32768)
-                bulk_load(reinterpret_cast<uint8_t *>(dst) + off,
-                          reinterpret_cast<const uint8_t *>(a.cbp[ph.mat]) + off,
-                          min(32768u, cbytes - off), &cbf[slot]);
-            q++;
-            const CUtensorMap *map = a.maps + ph.mat;
-            prefetch_tmap(map);
-            const int BN = 128 * ph.cpl, BR = mk_box_rows(ph.cpl, ph.nsub);
-            const int BW = BN / ph.nsub;
-            const int base = ph.K / ph.T, rem = ph.K % ph.T;
-            for (int i = cta; i < ph.ntasks; i += G) {
-                const int t = i / ph.ncb, j = i % ph.ncb;
-                const int k0 = t * base + min(t, rem), len = base + (t < rem ? 1 : 0);
-                const int nbox = (len + BR - 1) / BR;
-                for (int b = 0; b < nbox; b++, seq++) {
-                    const int s = seq % S;
-                    if (seq >= S && !mbar_wait(&empty[s], ((seq / S) - 1) & 1, a.status)) {
-                        atomicExch(a.abort, 1);
-                        return;
-                    }
-                    mbar_expect_tx(&full[s], MK_STAGE);
-                    uint8_t *d = ring + (size_t)s * MK_STAGE;
-                    if (ph.nsub == 1) {
-                        tma_load_2d(d, map, j * BN, k0 + b * BR, &full[s]);
-                    } else {
-                        tma_load_2d(d, map, j * BW, k0 + b * BR, &full[s]);
-                        tma_load_2d(d + MK_STAGE / 2, map, ph.F + j * BW, k0 + b * BR, &full[s]);
+            return;
+        }
+    }
+    if (warp == DS_PRODUCER) {
+        if (lane != 0) return;
+        int seq = 0;   // slot streams, in the consumers' order
+        const uint64_t pol = l2_evict_first();
+        for (int p = 0; p < a.nphases; p++) {
+            const DSPhase &ph = a.phases[p];
+            if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
+            if (ld_acquire(a.abort)) return;
+            const int M = (ph.ntasks - cta + G - 1) / G, ns = ph.d.ns, np = ph.npieces;
+            for (int r = 0; DS_NCW * r < M; r++) {
+                const int nr = min(DS_NCW, M - DS_NCW * r);
+                for (int b = 0; b < np; b++) {
+                    const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
+                    for (int m = DS_NCW * r; m < DS_NCW * r + nr; m++, seq++) {
+                        const int g = cta + m * G;
+                        const int s = seq % S;
+                        if (seq >= S && !mbar_wait(&empty[s], ((seq / S) - 1) & 1, a.status)) {
+                            atomicExch(a.abort, 1);
+                            return;
+                        }
+                        stage_seq[s] = seq;
+                        mbar_expect_tx(&full[s], bytes);
+                        bulk_load_hint(ring + (size_t)s * DS_STAGE,
+                                       ph.stream + ((size_t)g * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
+                                       bytes, &full[s], pol);
                     }
                 }
             }
@@ -230,316 +380,215 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_step(const __grid_cons
 
     // =============================================================== consumers
     const int tid = threadIdx.x;
-    int seq = 0, q = 0;
-    bool ok = true;
+    const int t = lane & 7, cp = lane >> 3;    // chunk, column pair
+    int seq_base = 0, q = 0;
+    float lm_v = -INFINITY;                    // this warp's first maximum
+    int lm_i = -1;
     for (int p = 0; p < a.nphases; p++) {
-        const MKPhase &ph = a.phases[p];
-        if (p > 0) {
-            if (tid == 0) s_last = mk_wait_counter(a.done + p - 1, G, a.status, a.abort) ? 1 : 0;
-            cbar_sync();
-            if (!s_last) {
-                ok = false;
-                break;
-            }
+        const DSPhase &ph = a.phases[p];
+        if (cta >= ph.ntasks) continue;
+        bool bad = false;
+        if (tid == 0) {
+            bool ok = !ld_acquire(a.abort);
+            if (ok && ph.dep >= 0) ok = ds_wait_counter(a.done + ph.dep, ph.dep_count, a.status, a.abort);
+            s_flag = ok ? 1 : 0;
         }
-        if (ph.kind == PH_GEMV) {
-            const bool mine = cta < ph.ntasks;
-            // ---------------------------------------------- norm prologue
-            if ((ph.xmode == PX_NORM_EMBED || ph.xmode == PX_NORM_RES) && (mine || cta == 0)) {
-                const int H = ph.K;
-                const float *src = nullptr;
-                if (ph.xmode == PX_NORM_EMBED) {
-                    if (tid == 0) {
-                        const int pos = a.st->pos, P = a.st->prompt_len;
-                        int tok = pos < P ? a.prompt[pos] : __ldcg(a.gen + pos - P);
-                        if (tok < 0 || tok >= a.vocab) {
-                            atomicOr(a.status, ST_BAD_TOKEN);
-                            tok = 0;
-                        }
-                        s_tok = tok;
-                    }
-                    cbar_sync();
-                    src = a.embed + (size_t)s_tok * H;
-                }
-                float ss = 0.f;
-                for (int i0 = tid; i0 < H; i0 += 4 * MK_NC) {
-                    float v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int i = i0 + u * MK_NC;
-                        if (i < H) {
-                            if (src) {
-                                v[u] = src[i];
-                            } else {
-                                float y = __ldcg(ph.xpart + i);
-                                for (int tt = 1; tt < ph.xpart_T; tt++)
-                                    y = __fadd_rn(y, __ldcg(ph.xpart + (size_t)tt * ph.xpart_N + i));
-                                v[u] = __fadd_rn(__ldcg(ph.x + i), y);
-                            }
-                        } else {
-                            v[u] = 0.f;
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int i = i0 + u * MK_NC;
-                        if (i < H) {
-                            hs[i] = v[u];
-                            ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
-                        }
-                    }
-                }
-                const float tot = mk_block_sum(ss, red);
+        cbar_sync();
+        if (!s_flag) break;   // uniform: every consumer warp leaves together
+        if (ph.kind == DS_GEMV) {
+            const TTXDesc &d = ph.d;
+            const int K = d.K, xs = ph.xs, xmode = ph.xmode;
+            // ------------------------------------------------ stage x
+            const float *src = ph.x;
+            if (xmode == DX_EMBED) {
                 if (tid == 0) {
-                    const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)H), ph.eps);
-                    s_rsq = (float)(1.0 / sqrt((double)add));
+                    int tok = ds_token(a);
+                    if (tok < 0) {
+                        atomicOr(a.status, ST_BAD_TOKEN);
+                        tok = 0;
+                    }
+                    s_tok = tok;
                 }
-                if (cta == 0)
-                    for (int i = tid; i < H; i += MK_NC) ph.h_out[i] = hs[i];
                 cbar_sync();
+                src = a.embed + (size_t)s_tok * K;
             }
-            if (mine) {
-                // A wait that gives up raises the abort flag and marks this
-                // thread bad: it skips the math but keeps every barrier and
-                // stage arrival, so no warp is left waiting; the phase
-                // boundary then ends the step uniformly.
-                const int slot = q & 1;
-                bool bad = !mbar_wait(&cbf[slot], (q >> 1) & 1, a.status);
-                if (bad) atomicExch(a.abort, 1);
-                const float *cb = cbs + (size_t)slot * a.cb_cap;
-                const int BN = 128 * ph.cpl, BR = mk_box_rows(ph.cpl, ph.nsub);
-                const int BW = BN / ph.nsub;
-                const int base = ph.K / ph.T, rem = ph.K % ph.T;
-                const float rsq = s_rsq;
-                const int wps = MK_NCW / ph.nsub;
-                const int qh = warp / wps;                       // half (nsub == 2)
-                const int wcol = (warp % wps) * 32 * ph.cpl + lane * ph.cpl;
-                const int rowstride = BW;
-                for (int i = cta; i < ph.ntasks; i += G) {
-                    const int t = i / ph.ncb, j = i % ph.ncb;
-                    const int k0 = t * base + min(t, rem), len = base + (t < rem ? 1 : 0);
-                    // x for the chunk's rows
-                    if (ph.xmode == PX_VEC) {
-                        for (int r = tid; r < len; r += MK_NC) xs[r] = __ldcg(ph.x + k0 + r);
-                    } else if (ph.xmode == PX_SWIGLU) {
-                        for (int r0 = tid; r0 < len; r0 += 2 * MK_NC) {
-                            float g[2], u[2];
+            // all of x (and the norm weights) in flight at once, then
+            // rmsnorm from registers: x * rsqrt(mean(x^2) + eps) * w
+            const bool norm = xmode != DX_VEC;
+            float ss = 0.f;
+            float v[DS_XU], w[DS_XU];
+            const bool one = K <= DS_XU * DS_NC;
+            for (int kb = 0; kb < K; kb += DS_XU * DS_NC) {
 #pragma unroll
-                            for (int e = 0; e < 2; e++) {
-                                const int r = r0 + e * MK_NC;
-                                g[e] = u[e] = 0.f;
-                                if (r < len) {
-                                    const float *pg = ph.xpart + k0 + r;
-                                    g[e] = __ldcg(pg);
-                                    u[e] = __ldcg(pg + ph.F);
-                                    for (int tt = 1; tt < ph.xpart_T; tt++) {
-                                        g[e] = __fadd_rn(g[e], __ldcg(pg + (size_t)tt * ph.xpart_N));
-                                        u[e] = __fadd_rn(u[e], __ldcg(pg + (size_t)tt * ph.xpart_N + ph.F));
-                                    }
-                                }
-                            }
+                for (int u = 0; u < DS_XU; u++) {
+                    const int k = kb + tid + u * DS_NC;
+                    v[u] = k < K ? __ldcg(src + k) : 0.f;
+                    w[u] = (norm && k < K) ? __ldg(ph.norm_w + k) : 0.f;
+                }
 #pragma unroll
-                            for (int e = 0; e < 2; e++) {
-                                const int r = r0 + e * MK_NC;
-                                if (r < len) {
-                                    const double d = (double)g[e];
-                                    xs[r] = __fmul_rn((float)(d / (1.0 + exp(-d))), u[e]);
-                                }
-                            }
-                        }
-                    } else {
-                        for (int r = tid; r < len; r += MK_NC)
-                            xs[r] = __fmul_rn(__fmul_rn(hs[k0 + r], rsq), __ldg(ph.norm_w + k0 + r));
+                for (int u = 0; u < DS_XU; u++) ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
+                if (!one || !norm) {   // stage x as is (scaled below when K is long)
+                    DSSlot sl(d, xs);
+#pragma unroll
+                    for (int u = 0; u < DS_XU; u++) {
+                        const int k = kb + tid + u * DS_NC;
+                        if (k < K) xc[sl.at(k)] = v[u];
                     }
-                    cbar_sync();
-                    // the chunk's rows, in order
-                    const int nbox = (len + BR - 1) / BR;
-                    float acc0 = 0.f, acc1 = 0.f;
-                    for (int b = 0; b < nbox; b++, seq++) {
-                        const int s = seq % S;
-                        if (!bad && !mbar_wait(&full[s], (seq / S) & 1, a.status)) {
-                            bad = true;
-                            atomicExch(a.abort, 1);
-                        }
-                        if (!bad) {
-                            const uint16_t *tile =
-                                reinterpret_cast<const uint16_t *>(
-                                    ring + (size_t)s * MK_STAGE +
-                                    (size_t)qh * (MK_STAGE / 2) * (ph.nsub - 1)) +
-                                wcol;
-                            const float *xb = xs + b * BR;
-                            const int rows = min(BR, len - b * BR);
-                            if (ph.cpl == 1) {
-                                if (rows == 64) {
-#pragma unroll 8
-                                    for (int r = 0; r < 64; r++)
-                                        acc0 = __fadd_rn(acc0, __fmul_rn(xb[r], cb[tile[r * rowstride]]));
-                                } else {
-                                    for (int r = 0; r < rows; r++)
-                                        acc0 = __fadd_rn(acc0, __fmul_rn(xb[r], cb[tile[r * rowstride]]));
-                                }
-                            } else {
-                                if (rows == 32) {
-#pragma unroll 8
-                                    for (int r = 0; r < 32; r++) {
-                                        const uint32_t w =
-                                            *reinterpret_cast<const uint32_t *>(tile + r * rowstride);
-                                        const float xv = xb[r];
-                                        acc0 = __fadd_rn(acc0, __fmul_rn(xv, cb[w & 0xffffu]));
-                                        acc1 = __fadd_rn(acc1, __fmul_rn(xv, cb[w >> 16]));
-                                    }
-                                } else {
-                                    for (int r = 0; r < rows; r++) {
-                                        const uint32_t w =
-                                            *reinterpret_cast<const uint32_t *>(tile + r * rowstride);
-                                        const float xv = xb[r];
-                                        acc0 = __fadd_rn(acc0, __fmul_rn(xv, cb[w & 0xffffu]));
-                                        acc1 = __fadd_rn(acc1, __fmul_rn(xv, cb[w >> 16]));
-                                    }
-                                }
-                            }
-                        }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&empty[s]);
+                }
+            }
+            if (norm) {
+                const float tot = ds_block_sum(ss, red);
+                const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)K), ph.eps);
+                const float rsq = (float)(1.0 / sqrt((double)add));
+                DSSlot sl(d, xs);
+                if (one) {
+#pragma unroll
+                    for (int u = 0; u < DS_XU; u++) {
+                        const int k = tid + u * DS_NC;
+                        if (k < K) xc[sl.at(k)] = __fmul_rn(__fmul_rn(v[u], rsq), w[u]);
                     }
-                    // partial row of this chunk
-                    int col;
-                    bool valid0, valid1;
-                    if (ph.nsub == 1) {
-                        col = j * BN + wcol;
-                        valid0 = col < ph.N;
-                        valid1 = col + 1 < ph.N;
-                    } else {
-                        const int c = j * BW + wcol;
-                        col = (qh == 0 ? 0 : ph.F) + c;
-                        valid0 = c < ph.F;
-                        valid1 = c + 1 < ph.F;
+                } else {
+                    for (int k = tid; k < K; k += DS_NC) {
+                        const int o = sl.at(k);
+                        xc[o] = __fmul_rn(__fmul_rn(xc[o], rsq), __ldg(ph.norm_w + k));
+                    }
+                }
+            }
+            cbar_sync();
+            const int slot = q & 1;
+            const float *tab = tabs + slot * a.tab_cap;
+            bad = !mbar_wait(&tready[slot], (q >> 1) & 1, a.status);
+            if (bad) atomicExch(a.abort, 1);
+            // ------------------------------------------------ tasks
+            const int M = (ph.ntasks - cta + G - 1) / G, ns = d.ns, np = ph.npieces;
+            const int len = d.chunk_len(t);
+            const int nfull = d.base / 8;             // steps inside every chunk
+            const float *xr = t < d.T ? xc + t * xs : xc;
+            const int pos = a.st->pos;
+            for (int m = warp; m < M; m += DS_NCW) {
+                const int r = m / DS_NCW, nr = min(DS_NCW, M - DS_NCW * r);
+                const int g = cta + m * G;
+                float2 acc = make_float2(0.f, 0.f);
+                for (int b = 0; b < np; b++) {
+                    const int seq = seq_base + r * DS_NCW * np + b * nr + (m - DS_NCW * r);
+                    const int s = seq % S;
+                    if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status) ||
+                                 !mbar_wait(&full[s], (seq / S) & 1, a.status))) {
+                        bad = true;
+                        atomicExch(a.abort, 1);
                     }
                     if (!bad) {
-                        float *out = ph.part + (size_t)t * ph.N + col;
-                        if (valid0) out[0] = acc0;
-                        if (ph.cpl == 2 && valid1) out[1] = acc1;
+                        const uint8_t *st = ring + (size_t)s * DS_STAGE;
+                        const int s0 = DS_PIECE_STEPS * b, s1 = min(ns, s0 + DS_PIECE_STEPS);
+                        const int sf = min(s1, max(s0, nfull));
+                        acc = ds_steps_full(st, lane, xr + 8 * s0, sf - s0, tab, acc);
+                        for (int sg = sf; sg < s1; sg++)
+                            acc = ds_step_tail(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
+                                               len - 8 * sg, tab, acc);
                     }
-                    cbar_sync();   // xs is rewritten by the next task
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&cbe[slot]);
-                q++;
-            }
-        } else if (ph.kind == PH_ATT) {
-            const int l = ph.layer, nkvh = a.nkv;
-            float *kcl = a.kc + (size_t)l * nkvh * a.max_pos * HD;
-            float *vcl = a.vc + (size_t)l * nkvh * a.max_pos * HD;
-            const int pos = a.st->pos;
-            const int qd = a.nh * HD, kvd = nkvh * HD;
-            for (int hq = cta; hq < ph.ntasks; hq += G) {
-                const int g = hq / a.groups;
-                if (pos >= a.max_pos) break;
-                for (int i = tid; i < 3 * HD; i += MK_NC) {
-                    const int which = i / HD, d = i % HD;
-                    const int col = which == 0 ? hq * HD + d
-                                               : (which == 1 ? qd + g * HD + d : qd + kvd + g * HD + d);
-                    float v = __ldcg(a.qkv_part + col);
-                    for (int tt = 1; tt < a.qkv_T; tt++)
-                        v = __fadd_rn(v, __ldcg(a.qkv_part + (size_t)tt * a.nq + col));
-                    (which == 0 ? qv : which == 1 ? kv : vv)[d] = v;
+                // chunk sums in chunk order
+                float2 y;
+                y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
+                y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
+                for (int tt = 1; tt < d.T; tt++) {
+                    float2 o;
+                    o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
+                    o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
+                    y = __fadd2_rn(y, o);
                 }
-                cbar_sync();
-                float qr = 0.f, kr = 0.f;
-                for (int d = tid; d < HD; d += MK_NC) {
-                    const float c = a.rope_cos[(size_t)pos * HD + d];
-                    const float s = a.rope_sin[(size_t)pos * HD + d];
-                    const int half = HD / 2;
-                    const float rq = d < half ? -qv[d + half] : qv[d - half];
-                    const float rk = d < half ? -kv[d + half] : kv[d - half];
-                    qr = __fadd_rn(__fmul_rn(qv[d], c), __fmul_rn(rq, s));
-                    kr = __fadd_rn(__fmul_rn(kv[d], c), __fmul_rn(rk, s));
-                }
-                cbar_sync();
-                for (int d = tid; d < HD; d += MK_NC) {
-                    qv[d] = qr;
-                    kv[d] = kr;
-                    if (hq % a.groups == 0) {
-                        const size_t o = ((size_t)g * a.max_pos + pos) * HD + d;
-                        kcl[o] = kr;
-                        vcl[o] = vv[d];
-                    }
-                }
-                cbar_sync();
-                constexpr int DPL = HD / 32;
-                float qreg[DPL];
+                const int n0 = ttx_col(d, g, 2 * cp), n1 = ttx_col(d, g, 2 * cp + 1);
+                if (ph.emode == DE_QKV) {
+                    float2 pr;   // rotate-half partner (pair cp ^ 2)
+                    pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
+                    pr.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
+                    if (t == 0 && !bad && pos < a.max_pos) {
+                        const bool rot = g < d.rope_heads * (HD / 8);
+                        const float yy[2] = {y.x, y.y}, pp[2] = {pr.x, pr.y};
+                        const int nn[2] = {n0, n1};
 #pragma unroll
-                for (int e = 0; e < DPL; e++) qreg[e] = qv[lane + 32 * e];
-                for (int jj = warp; jj <= pos; jj += MK_NCW) {
-                    const float *kj = jj == pos ? kv : kcl + ((size_t)g * a.max_pos + jj) * HD;
-                    float dot = __fmul_rn(qreg[0], jj == pos ? kj[lane] : __ldcg(kj + lane));
+                        for (int k = 0; k < 2; k++) {
+                            const int n = nn[k];
+                            if (n < 0) continue;
+                            if (rot) {
+                                const int head = n / HD, dim = n % HD;
+                                const float rt = cp < 2 ? -pp[k] : pp[k];
+                                const float c = __ldg(a.rope_cos + (size_t)pos * HD + dim);
+                                const float sn = __ldg(a.rope_sin + (size_t)pos * HD + dim);
+                                const float v = __fadd_rn(__fmul_rn(yy[k], c), __fmul_rn(rt, sn));
+                                if (head < a.nh)
+                                    a.q[n] = v;
+                                else
+                                    a.kc[(((size_t)ph.layer * a.nkv + (head - a.nh)) * a.max_pos + pos) * HD + dim] = v;
+                            } else {
+                                const int vi = n - a.qd - a.kvd;
+                                a.vc[(((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD] = yy[k];
+                            }
+                        }
+                    }
+                } else if (ph.emode == DE_RESID) {
+                    if (t == 0 && !bad) {
+                        const float yy[2] = {y.x, y.y};
+                        const int nn[2] = {n0, n1};
+                        int tok = 0;
+                        if (!ph.hold) {
+                            tok = ds_token(a);
+                            tok = tok < 0 ? 0 : tok;
+                        }
 #pragma unroll
-                    for (int e = 1; e < DPL; e++)
-                        dot = __fadd_rn(dot, __fmul_rn(qreg[e], jj == pos ? kj[lane + 32 * e]
-                                                                          : __ldcg(kj + lane + 32 * e)));
-                    for (int o = 16; o; o >>= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, o));
-                    if (lane == 0) sc[jj] = __fmul_rn(dot, a.scale);
-                }
-                cbar_sync();
-                float m = -INFINITY;
-                for (int jj = tid; jj <= pos; jj += MK_NC) m = fmaxf(m, sc[jj]);
-                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                if (lane == 0) red[warp] = m;
-                cbar_sync();
-                float mx = red[0];
-                for (int w2 = 1; w2 < MK_NCW; w2++) mx = fmaxf(mx, red[w2]);
-                float sum = 0.f;
-                for (int jj = tid; jj <= pos; jj += MK_NC) {
-                    const float e = (float)exp((double)__fsub_rn(sc[jj], mx));
-                    sc[jj] = e;
-                    sum = __fadd_rn(sum, e);
-                }
-                cbar_sync();   // everyone has read red[] (max) before it is reused
-                const float tot = mk_block_sum(sum, red);
-                for (int jj = tid; jj <= pos; jj += MK_NC) sc[jj] = __fdiv_rn(sc[jj], tot);
-                cbar_sync();
-                constexpr int NG = MK_NC / HD > 0 ? MK_NC / HD : 1;
-                for (int d0 = tid % HD; d0 < HD; d0 += MK_NC) {
-                    const int grp = tid / HD;
-                    float acc = 0.f;
-                    for (int jj = grp; jj <= pos; jj += NG) {
-                        const float vj = jj == pos ? vv[d0]
-                                                   : __ldcg(vcl + ((size_t)g * a.max_pos + jj) * HD + d0);
-                        acc = __fadd_rn(acc, __fmul_rn(sc[jj], vj));
+                        for (int k = 0; k < 2; k++) {
+                            const int n = nn[k];
+                            if (n < 0) continue;
+                            const float h0 = ph.hold ? __ldcg(ph.hold + n)
+                                                     : __ldg(a.embed + (size_t)tok * a.H + n);
+                            ph.out[n] = __fadd_rn(h0, yy[k]);
+                        }
                     }
-                    if (grp < NG) pctx[grp][d0] = acc;
+                } else if (ph.emode == DE_SWIGLU) {
+                    float2 up;
+                    up.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
+                    up.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
+                    if (t == 0 && cp < 2 && !bad) {
+                        const float yy[2] = {y.x, y.y}, uu[2] = {up.x, up.y};
+                        const int nn[2] = {n0, n1};
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            if (nn[k] < 0) continue;
+                            const double dg = (double)yy[k];
+                            ph.out[nn[k]] = __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]);
+                        }
+                    }
+                } else {   // DE_LM
+                    if (t == 0 && !bad) {
+                        const float yy[2] = {y.x, y.y};
+                        const int nn[2] = {n0, n1};
+#pragma unroll
+                        for (int k = 0; k < 2; k++) {
+                            const int n = nn[k];
+                            if (n < 0) continue;
+                            ph.out[n] = yy[k];
+                            if (a.hist && pos < a.hist_rows) a.hist[(size_t)pos * d.N + n] = yy[k];
+                            if (yy[k] > lm_v || (yy[k] == lm_v && lm_i >= 0 && n < lm_i)) {
+                                lm_v = yy[k];
+                                lm_i = n;
+                            }
+                        }
+                    }
                 }
-                cbar_sync();
-                for (int d = tid; d < HD; d += MK_NC) {
-                    float acc = pctx[0][d];
-                    for (int i = 1; i < NG; i++) acc = __fadd_rn(acc, pctx[i][d]);
-                    a.ctx[hq * HD + d] = acc;
-                }
-                cbar_sync();
             }
-        } else {   // PH_ARGMAX
-            const int V = a.vocab;
-            const int per = (V + ph.ntasks - 1) / ph.ntasks;
-            const int pos = a.st->pos;
-            for (int sl = cta; sl < ph.ntasks; sl += G) {
-                const int v0 = sl * per, v1 = min(V, v0 + per);
-                float bv = -INFINITY;
-                int bi = 0x7fffffff;
-                for (int v = v0 + tid; v < v1; v += MK_NC) {
-                    float y = __ldcg(a.lm_part + v);
-                    for (int tt = 1; tt < a.lm_T; tt++)
-                        y = __fadd_rn(y, __ldcg(a.lm_part + (size_t)tt * V + v));
-                    a.logits[v] = y;
-                    if (a.hist && pos < a.hist_rows) a.hist[(size_t)pos * V + v] = y;
-                    if (y > bv || bi == 0x7fffffff) {
-                        bv = y;
-                        bi = v;
-                    }
-                }
+            seq_base += M * np;
+            cbar_sync();   // every warp's outputs are stored and the table is free
+            if (tid == 0) mbar_arrive(&tfree[slot]);
+            q++;
+            if (ph.emode == DE_LM) {   // this CTA's first maximum
+                float bv = lm_v;
+                int bi = lm_i;
                 for (int o = 16; o; o >>= 1) {
                     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > bv || (ov == bv && oi < bi)) {
+                    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
                         bv = ov;
                         bi = oi;
                     }
@@ -550,50 +599,144 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_step(const __grid_cons
                 }
                 cbar_sync();
                 if (tid == 0) {
-                    for (int w2 = 1; w2 < MK_NCW; w2++)
-                        if (red[w2] > bv || (red[w2] == bv && ri[w2] < bi)) {
-                            bv = red[w2];
-                            bi = ri[w2];
+                    for (int w2 = 1; w2 < DS_NCW; w2++) {
+                        const int oi = ri[w2];
+                        const float ov = red[w2];
+                        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+                            bv = ov;
+                            bi = oi;
                         }
-                    a.cand_v[sl] = bv;
-                    a.cand_i[sl] = bi;
+                    }
+                    a.cand_v[cta] = bv;
+                    a.cand_i[cta] = bi;
+                }
+            }
+            if (tid == 0) {
+                __threadfence();
+                const int prev = atomicAdd(a.done + p, 1);
+                const int ncta = min(G, ph.ntasks);
+                if (ph.emode == DE_LM && prev == ncta - 1) {
+                    // the reference's greedy pick: best = logits[0], then
+                    // strict > over the rest in index order
+                    __threadfence();
+                    const float l0 = __ldcg(ph.out);
+                    int bidx = 0;
+                    if (!(l0 != l0)) {
+                        float best = l0;
+                        for (int c = 0; c < ncta; c++) {
+                            const float cv = __ldcg(a.cand_v + c);
+                            const int ci = __ldcg(a.cand_i + c);
+                            if (ci >= 0 && (cv > best || (cv == best && ci < bidx))) {
+                                best = cv;
+                                bidx = ci;
+                            }
+                        }
+                    }
+                    const int P0 = a.st->prompt_len;
+                    if (pos >= P0 - 1) {
+                        const int gi = pos - (P0 - 1);
+                        if (gi < a.max_gen) {
+                            a.gen[gi] = bidx;
+                            a.gen_host[gi] = bidx;
+                            __threadfence_system();
+                        }
+                        a.st->n_gen = gi + 1;
+                    }
+                    a.st->pos = pos + 1;
+                }
+            }
+        } else {   // ============================================ attention
+            const int l = ph.layer;
+            const float *kcl = a.kc + (size_t)l * a.nkv * a.max_pos * HD;
+            const float *vcl = a.vc + (size_t)l * a.nkv * a.max_pos * HD;
+            const int pos = a.st->pos;
+            for (int hq = cta; hq < ph.ntasks; hq += G) {
+                const int g = hq / a.groups;
+                if (pos < a.max_pos) {
+                    for (int d = tid; d < HD; d += DS_NC) qv[d] = __ldcg(a.q + hq * HD + d);
+                    cbar_sync();
+                    const float4 *q4 = reinterpret_cast<const float4 *>(qv);
+                    for (int jj = tid; jj <= pos; jj += DS_NC) {
+                        const float4 *kg4 =
+                            reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD);
+                        float dot = 0.f;
+#pragma unroll
+                        for (int e0 = 0; e0 < NQ; e0 += 8) {
+                            float4 kk[8];
+#pragma unroll
+                            for (int e = 0; e < 8; e++) kk[e] = __ldcg(kg4 + e0 + e);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                const float4 qq = q4[e0 + e];
+                                dot = __fadd_rn(dot, __fmul_rn(qq.x, kk[e].x));
+                                dot = __fadd_rn(dot, __fmul_rn(qq.y, kk[e].y));
+                                dot = __fadd_rn(dot, __fmul_rn(qq.z, kk[e].z));
+                                dot = __fadd_rn(dot, __fmul_rn(qq.w, kk[e].w));
+                            }
+                        }
+                        sc[jj] = __fmul_rn(dot, a.scale);
+                    }
+                    cbar_sync();
+                    float m = -INFINITY;
+                    for (int jj = tid; jj <= pos; jj += DS_NC) m = fmaxf(m, sc[jj]);
+                    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    if (lane == 0) red[warp] = m;
+                    cbar_sync();
+                    float mx = red[0];
+                    for (int w2 = 1; w2 < DS_NCW; w2++) mx = fmaxf(mx, red[w2]);
+                    float sum = 0.f;
+                    for (int jj = tid; jj <= pos; jj += DS_NC) {
+                        const float e = (float)exp((double)__fsub_rn(sc[jj], mx));
+                        sc[jj] = e;
+                        sum = __fadd_rn(sum, e);
+                    }
+                    const float tot = ds_block_sum(sum, red);
+                    for (int jj = tid; jj <= pos; jj += DS_NC) sc[jj] = __fdiv_rn(sc[jj], tot);
+                    cbar_sync();
+                    {   // P.V: thread = (dim quad, position group), 4 positions in flight
+                        const int dq = tid % NQ, pg = tid / NQ;
+                        const float4 *vg4 =
+                            reinterpret_cast<const float4 *>(vcl + (size_t)g * a.max_pos * HD) + dq;
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        int jj = pg;
+                        for (; jj + 3 * NPG <= pos; jj += 4 * NPG) {
+                            float4 vj[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) vj[e] = __ldcg(vg4 + (size_t)(jj + e * NPG) * NQ);
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const float pj = sc[jj + e * NPG];
+                                acc.x = __fadd_rn(acc.x, __fmul_rn(pj, vj[e].x));
+                                acc.y = __fadd_rn(acc.y, __fmul_rn(pj, vj[e].y));
+                                acc.z = __fadd_rn(acc.z, __fmul_rn(pj, vj[e].z));
+                                acc.w = __fadd_rn(acc.w, __fmul_rn(pj, vj[e].w));
+                            }
+                        }
+                        for (; jj <= pos; jj += NPG) {
+                            const float4 vj = __ldcg(vg4 + (size_t)jj * NQ);
+                            const float pj = sc[jj];
+                            acc.x = __fadd_rn(acc.x, __fmul_rn(pj, vj.x));
+                            acc.y = __fadd_rn(acc.y, __fmul_rn(pj, vj.y));
+                            acc.z = __fadd_rn(acc.z, __fmul_rn(pj, vj.z));
+                            acc.w = __fadd_rn(acc.w, __fmul_rn(pj, vj.w));
+                        }
+                        reinterpret_cast<float4 *>(pctx[pg])[dq] = acc;
+                    }
+                    cbar_sync();
+                    for (int d = tid; d < HD; d += DS_NC) {
+                        float acc = pctx[0][d];
+                        for (int i2 = 1; i2 < NPG; i2++) acc = __fadd_rn(acc, pctx[i2][d]);
+                        a.ctx[hq * HD + d] = acc;
+                    }
                 }
                 cbar_sync();
-            }
-        }
-        // ------------------------------------------------------ arrival
-        cbar_sync();
-        if (tid == 0) {
-            __threadfence();
-            const int prev = atomicAdd(a.done + p, 1);
-            if (ph.kind == PH_ARGMAX && prev == G - 1) {
-                __threadfence();
-                float best = __ldcg(a.cand_v);
-                int bidx = __ldcg(a.cand_i);
-                for (int j = 1; j < ph.ntasks; j++) {
-                    const float cv = __ldcg(a.cand_v + j);
-                    const int ci = __ldcg(a.cand_i + j);
-                    if (cv > best || (cv == best && ci < bidx)) {
-                        best = cv;
-                        bidx = ci;
-                    }
+                if (tid == 0) {
+                    __threadfence();
+                    atomicAdd(a.done + p, 1);
                 }
-                if (bidx < 0 || bidx >= a.vocab) bidx = 0;
-                const int pos = a.st->pos, P0 = a.st->prompt_len;
-                if (pos >= P0 - 1) {
-                    const int gi = pos - (P0 - 1);
-                    if (gi < a.max_gen) {
-                        a.gen[gi] = bidx;
-                        a.gen_host[gi] = bidx;
-                        __threadfence_system();
-                    }
-                    a.st->n_gen = gi + 1;
-                }
-                a.st->pos = pos + 1;
             }
         }
     }
-    if (!ok && tid == 0) atomicExch(a.abort, 1);
 }
 
 }  // namespace kllm

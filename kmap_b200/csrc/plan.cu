@@ -369,9 +369,7 @@ k_attention(const StepState *st, const float *__restrict__ qkv_part, int T, int 
     for (int i = tid; i < 3 * HD; i += THREADS) {
         int which = i / HD, d = i % HD;
         int col = which == 0 ? hq * HD + d : (which == 1 ? qd + g * HD + d : qd + kvd + g * HD + d);
-        float a = qkv_part[col];
-        for (int t = 1; t < T; t++) a = __fadd_rn(a, qkv_part[(size_t)t * nq + col]);
-        (which == 0 ? q : which == 1 ? k : v)[d] = a;
+        (which == 0 ? q : which == 1 ? k : v)[d] = sum_parts(qkv_part + col, nq, T);
     }
     __syncthreads();
     // RoPE: x*cos + rotate_half(x)*sin, rotate_half = concat(-x2, x1)
@@ -488,17 +486,15 @@ struct DecodePlan {
     float *graph_hist = nullptr;   // history buffer baked into the graph
     // persistent step kernel
     bool persist = false;
-    int mk_grid = 0, mk_stages = 0;
-    size_t mk_smem = 0;
-    MKArgs mk = {};
-    std::vector<MKPhase> phases;
-    MKPhase *d_phases = nullptr;
-    CUtensorMap *d_maps = nullptr;
-    const float **d_cbp = nullptr;
-    int *d_ncodes = nullptr;
-    int *d_done = nullptr, *d_abort = nullptr;
-    float *hbuf = nullptr;            // [2][H] residual versions
-    float *pq = nullptr, *po = nullptr, *pg = nullptr, *pd = nullptr, *pl = nullptr;
+    int ds_grid = 0, ds_stages = 0;
+    size_t ds_smem = 0;
+    DSArgs ds = {};
+    std::vector<DSPhase> phases;
+    DSPhase *d_phases = nullptr;
+    int *d_cnt = nullptr;          // done[phases] + tile counters, zeroed per step
+    size_t cnt_n = 0;
+    int *d_abort = nullptr;
+    std::vector<void *> ds_bufs;   // device layouts, partials, activations
     long long kernels_per_step = 0;
     int graph_hist_rows = 0;
     int logits_slot = -1;
@@ -517,9 +513,9 @@ static void free_plan(DecodePlan *p) {
         if (b) cudaFree(b);
     for (float *b : p->dev_norm)
         if (b) cudaFree(b);
-    void *mbufs[] = {p->d_phases, p->d_maps, p->d_cbp, p->d_ncodes, p->d_done, p->d_abort,
-                     p->hbuf, p->pq, p->po, p->pg, p->pd, p->pl};
-    for (void *b : mbufs)
+    for (void *b : p->ds_bufs)
+        if (b) cudaFree(b);
+    for (void *b : {(void *)p->d_phases, (void *)p->d_cnt, (void *)p->d_abort})
         if (b) cudaFree(b);
     if (p->gen_host) cudaFreeHost(p->gen_host);
     for (cudaEvent_t e : {p->ev0, p->ev1, p->ev2})
@@ -555,138 +551,145 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     if (!env_on("KLLM_PERSIST", true)) return false;
     const TapeCtx *ctx = &c->base;
     const TemplateInfo &t = p->ti;
-    const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, nq = qd + 2 * nkv * hd;
-    const int F = t.F, V = t.V, L = t.L;
+    const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, kvd = nkv * hd;
+    const int V = t.V, L = t.L;
     const int nmat = (int)tts.size();
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
-    // geometry per matrix role: cpl / nsub
-    auto role_of = [&](int i) { return i + 1 == nmat ? 4 : i % 4; };   // 0 qkv 1 o 2 gu 3 dn 4 lm
-    auto cpl_of = [](int r) { return (r == 2 || r == 4) ? 2 : 1; };
-    auto nsub_of = [](int r) { return r == 2 ? 2 : 1; };
-    // tensor maps (box per role)
-    std::vector<CUtensorMap> maps(nmat);
-    std::vector<const float *> cbp(nmat);
-    std::vector<int> ncodes(nmat);
-    int cb_cap = 4;
+    auto kern = hd == 32 ? k_decode_step<32> : hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    cudaFuncAttributes fa = {};
+    if (!KLLM_CUDA(cudaFuncGetAttributes(&fa, kern))) return false;
+    int smem_optin = 0;
+    cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device);
+    const size_t avail = (size_t)smem_optin - fa.sharedSizeBytes;
+    // device layouts (ttx.cuh), one per matrix
+    // two tables (this phase's and the next's), R <= 2 copies each
+    int max_r = 2;
+    if (const char *e = getenv("KLLM_TTX_R")) max_r = std::max(1, std::min(4, atoi(e)));
+    const int max_table = 48 * 1024;
+    std::vector<TTXDesc> desc(nmat);
+    std::vector<uint8_t *> streams(nmat);
+    std::vector<int> xsz(nmat);
+    int tab_cap = 0, xc_cap = (p->max_pos + 3) & ~3;
+    auto own = [&](void *b) { p->ds_bufs.push_back(b); };
     for (int i = 0; i < nmat; i++) {
         const Slot &sl = ctx->slots[tts[i]];
         const DevSlot &w = c->ds[tts[i]];
-        const int r = role_of(i), cpl = cpl_of(r), nsub = nsub_of(r);
-        const int bw = 128 * cpl / nsub, br = mk_box_rows(cpl, nsub);
-        if (sl.tt_N % 8 || ((uintptr_t)w.d_idx % 16) || ((uintptr_t)w.d_cb % 16)) return false;
-        if (!make_idx_tmap(&maps[i], w.d_idx, sl.tt_K, sl.tt_N, bw, br)) return false;
-        cbp[i] = w.d_cb;
-        ncodes[i] = sl.n_codes;
-        cb_cap = std::max(cb_cap, (sl.n_codes + 3) & ~3);
+        const int role = i + 1 == nmat ? 4 : i % 4;   // 0 qkv 1 o 2 gate_up 3 down 4 lm_head
+        const int mode = role == 0 ? TTX_ROPE : role == 2 ? TTX_GATE_UP : TTX_IDENT;
+        if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, hd, t.nh + nkv, max_table, max_r,
+                          &desc[i]))
+            return false;
+        const TTXDesc &d = desc[i];
+        if (!KLLM_CUDA(cudaMalloc((void **)&streams[i], d.stream_bytes()))) return false;
+        own(streams[i]);
+        if (!ttx_build(c->stream, w.d_idx, w.d_cb, d, streams[i], nullptr)) return false;
+        tab_cap = std::max(tab_cap, (int)d.table_elems());
+        // staged x: chunk rows of 8 * ns floats, padded to 4 mod 32 floats so
+        // that the 8 chunks' float4 reads fall in different banks
+        const int r8 = 8 * d.ns;
+        xsz[i] = r8 + ((4 - r8 % 32) + 32) % 32;
+        xc_cap = std::max(xc_cap, d.T * xsz[i]);
     }
-    const int T_h = tt_chunks(H), T_qd = tt_chunks(qd), T_f = tt_chunks(F);
-    const int max_len = std::max({(H + T_h - 1) / T_h, (qd + T_qd - 1) / T_qd, (F + T_f - 1) / T_f});
-    const int h_cap = (H + 3) & ~3, xs_cap = (max_len + 3) & ~3, sc_cap = (p->max_pos + 3) & ~3;
-    const size_t fixed = (size_t)4 * (2 * cb_cap + h_cap + xs_cap + sc_cap) + 64;
-    const size_t budget = 220 * 1024;
-    if (fixed + 2 * (MK_STAGE + 16) > budget) return false;
-    const int S = (int)std::min<size_t>(24, (budget - fixed) / (MK_STAGE + 16));
-    const size_t smem = (size_t)S * (MK_STAGE + 16) + fixed;
-    auto kern = hd == 32 ? k_decode_step<32> : hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    if (!KLLM_CUDA(cudaStreamSynchronize(c->stream))) return false;
+    // shared memory: ring | 2 tables | staged x (attention scores alias
+    // it) | mbarriers
+    xc_cap = (xc_cap + 3) & ~3;
+    const size_t fixed = (size_t)4 * (2 * tab_cap + xc_cap) + 8 * 5 + 16;
+    if (avail <= fixed + 2 * ((size_t)DS_STAGE + 16)) return false;
+    const int S = (int)std::min<size_t>(DS_MAX_STAGES, (avail - fixed) / (DS_STAGE + 20));
+    const size_t smem = (size_t)S * DS_STAGE + fixed + (size_t)8 * (2 * S) + (size_t)4 * S;
+    if (S < 2 || smem > avail) return false;
     if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem)))
         return false;
     int per_sm = 0;
-    if (!KLLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, MK_THREADS, smem)) ||
+    if (!KLLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DS_THREADS, smem)) ||
         per_sm < 1)
         return false;
-    // scratch
-    auto fa = [&](float **b, size_t n) { return dalloc(b, n); };
-    if (!fa(&p->hbuf, 2 * (size_t)H) || !fa(&p->pq, (size_t)T_h * nq) ||
-        !fa(&p->po, (size_t)T_qd * H) || !fa(&p->pg, (size_t)T_h * 2 * F) ||
-        !fa(&p->pd, (size_t)T_f * H) || !fa(&p->pl, (size_t)T_h * V))
-        return false;
+    // activations
+    auto fbuf = [&](size_t n) -> float * {
+        float *b = nullptr;
+        if (!KLLM_CUDA(cudaMalloc((void **)&b, std::max<size_t>(n, 1) * 4))) return nullptr;
+        own(b);
+        return b;
+    };
+    float *qb = fbuf(qd), *act = fbuf(t.F), *hA = fbuf(H), *hB = fbuf(H);
+    if (!qb || !act || !hA || !hB) return false;
+    if (sms > 1024) return false;   // lm_head candidates, one per CTA
     // phases
-    std::vector<MKPhase> ph;
-    auto gemv = [&](int mi, int K, int N, int xmode, const float *x, const float *xpart,
-                    int xT, int xN, const float *nw, float eps, float *hout, float *part) {
-        MKPhase m = {};
-        const int r = role_of(mi), cpl = cpl_of(r), nsub = nsub_of(r);
-        m.kind = PH_GEMV;
-        m.mat = mi;
-        m.K = K;
-        m.N = N;
-        m.T = tt_chunks(K);
-        m.cpl = cpl;
-        m.nsub = nsub;
-        m.F = F;
-        m.ncb = nsub == 2 ? (F + 127) / 128 : (N + 128 * cpl - 1) / (128 * cpl);
-        m.ntasks = m.ncb * m.T;
+    std::vector<DSPhase> ph;
+    auto ncta = [&](int ntasks) { return std::min(sms, ntasks); };
+    auto gemv = [&](int mi, int xmode, const float *x, const float *nw, float eps, int emode,
+                    const float *hold, float *out, int dep, int dep_count, int layer) {
+        const TTXDesc &d = desc[mi];
+        DSPhase m = {};
+        m.kind = DS_GEMV;
+        m.ntasks = d.ngroups;
+        m.dep = dep;
+        m.dep_count = dep_count;
+        m.d = d;
+        m.npieces = (d.ns + DS_PIECE_STEPS - 1) / DS_PIECE_STEPS;
+        m.xs = xsz[mi];
+        m.stream = streams[mi];
+        m.cb = c->ds[tts[mi]].d_cb;
+        m.cb_bytes = ((d.n_codes + 3) & ~3) * 4;
         m.xmode = xmode;
+        m.emode = emode;
         m.x = x;
-        m.xpart = xpart;
-        m.xpart_T = xT;
-        m.xpart_N = xN;
         m.norm_w = nw;
         m.eps = eps;
-        m.h_out = hout;
-        m.part = part;
+        m.hold = hold;
+        m.out = out;
+        m.layer = layer;
         ph.push_back(m);
+        return (int)ph.size() - 1;
     };
-    float *hb[2] = {p->hbuf, p->hbuf + H};
+    int prev_dn = -1;
     for (int l = 0; l < L; l++) {
-        if (l == 0)
-            gemv(4 * l, H, nq, PX_NORM_EMBED, nullptr, nullptr, 0, 0, p->dev_norm[2 * l],
-                 p->eps[2 * l], hb[0], p->pq);
-        else
-            gemv(4 * l, H, nq, PX_NORM_RES, hb[1], p->pd, T_f, H, p->dev_norm[2 * l],
-                 p->eps[2 * l], hb[0], p->pq);
-        MKPhase at = {};
-        at.kind = PH_ATT;
+        const int mq = 4 * l;
+        const int p_qkv =
+            l == 0 ? gemv(mq, DX_EMBED, nullptr, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr,
+                          qb, -1, 0, l)
+                   : gemv(mq, DX_NORM, hA, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr, qb,
+                          prev_dn, ncta(desc[mq - 1].ngroups), l);
+        DSPhase at = {};
+        at.kind = DS_ATT;
         at.ntasks = t.nh;
+        at.dep = p_qkv;
+        at.dep_count = ncta(desc[mq].ngroups);
         at.layer = l;
         ph.push_back(at);
-        gemv(4 * l + 1, qd, H, PX_VEC, p->ctx, nullptr, 0, 0, nullptr, 0.f, nullptr, p->po);
-        gemv(4 * l + 2, H, 2 * F, PX_NORM_RES, hb[0], p->po, T_qd, H, p->dev_norm[2 * l + 1],
-             p->eps[2 * l + 1], hb[1], p->pg);
-        gemv(4 * l + 3, F, H, PX_SWIGLU, nullptr, p->pg, T_h, 2 * F, nullptr, 0.f, nullptr, p->pd);
+        const int p_att = (int)ph.size() - 1;
+        const int p_o = gemv(mq + 1, DX_VEC, p->ctx, nullptr, 0.f, DE_RESID, l == 0 ? nullptr : hA,
+                             hB, p_att, t.nh, l);
+        const int p_gu = gemv(mq + 2, DX_NORM, hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1],
+                              DE_SWIGLU, nullptr, act, p_o, ncta(desc[mq + 1].ngroups), l);
+        prev_dn = gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, hB, hA, p_gu,
+                       ncta(desc[mq + 2].ngroups), l);
     }
-    gemv(nmat - 1, H, V, PX_NORM_RES, hb[1], p->pd, T_f, H, p->dev_norm.back(), p->f_eps, hb[0],
-         p->pl);
-    MKPhase am = {};
-    am.kind = PH_ARGMAX;
-    am.ntasks = std::min(sms, 1024);
-    ph.push_back(am);
-    // device copies
-    if (!KLLM_CUDA(cudaMalloc((void **)&p->d_phases, ph.size() * sizeof(MKPhase))) ||
-        !KLLM_CUDA(cudaMemcpy(p->d_phases, ph.data(), ph.size() * sizeof(MKPhase),
+    gemv(nmat - 1, DX_NORM, hA, p->dev_norm.back(), p->f_eps, DE_LM, nullptr, p->logits, prev_dn,
+         ncta(desc[nmat - 2].ngroups), L);
+    const size_t nph = ph.size();
+    p->cnt_n = nph;
+    if (!KLLM_CUDA(cudaMalloc((void **)&p->d_cnt, p->cnt_n * sizeof(int))) ||
+        !KLLM_CUDA(cudaMemset(p->d_cnt, 0, p->cnt_n * sizeof(int))) ||
+        !KLLM_CUDA(cudaMalloc((void **)&p->d_phases, nph * sizeof(DSPhase))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_phases, ph.data(), nph * sizeof(DSPhase),
                               cudaMemcpyHostToDevice)) ||
-        !KLLM_CUDA(cudaMalloc((void **)&p->d_maps, nmat * sizeof(CUtensorMap))) ||
-        !KLLM_CUDA(cudaMemcpy(p->d_maps, maps.data(), nmat * sizeof(CUtensorMap),
-                              cudaMemcpyHostToDevice)) ||
-        !KLLM_CUDA(cudaMalloc((void **)&p->d_cbp, nmat * sizeof(float *))) ||
-        !KLLM_CUDA(cudaMemcpy(p->d_cbp, cbp.data(), nmat * sizeof(float *),
-                              cudaMemcpyHostToDevice)) ||
-        !KLLM_CUDA(cudaMalloc((void **)&p->d_ncodes, nmat * sizeof(int))) ||
-        !KLLM_CUDA(cudaMemcpy(p->d_ncodes, ncodes.data(), nmat * sizeof(int),
-                              cudaMemcpyHostToDevice)) ||
-        !KLLM_CUDA(cudaMalloc((void **)&p->d_done, (ph.size() + 1) * sizeof(int))) ||
         !KLLM_CUDA(cudaMalloc((void **)&p->d_abort, sizeof(int))) ||
         !KLLM_CUDA(cudaMemset(p->d_abort, 0, sizeof(int))))
         return false;
-    if (((uintptr_t)p->d_maps % 64) != 0) return false;
     p->phases = ph;
-    MKArgs &a = p->mk;
+    DSArgs &a = p->ds;
     a.phases = p->d_phases;
-    a.nphases = (int)ph.size();
-    a.maps = p->d_maps;
-    a.cbp = p->d_cbp;
-    a.ncodes = p->d_ncodes;
-    a.done = p->d_done;
+    a.nphases = (int)nph;
+    a.done = p->d_cnt;
     a.status = p->status;
     a.abort = p->d_abort;
     a.stages = S;
-    a.cb_cap = cb_cap;
-    a.h_cap = h_cap;
-    a.xs_cap = xs_cap;
-    a.sc_cap = sc_cap;
-    a.H = H;
+    a.tab_cap = tab_cap;
+    a.xc_cap = xc_cap;
     a.st = p->st;
     a.embed = p->embed;
     a.prompt = p->prompt;
@@ -694,27 +697,25 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.gen_host = (volatile int *)p->gen_host_dev;
     a.vocab = V;
     a.max_gen = p->max_pos;
-    a.qkv_part = p->pq;
-    a.qkv_T = T_h;
-    a.nq = nq;
+    a.H = H;
+    a.q = qb;
     a.nh = t.nh;
     a.nkv = nkv;
     a.groups = t.groups;
     a.max_pos = p->max_pos;
+    a.qd = qd;
+    a.kvd = kvd;
     a.rope_cos = p->rcos;
     a.rope_sin = p->rsin;
     a.kc = p->kc;
     a.vc = p->vc;
     a.scale = p->scale;
     a.ctx = p->ctx;
-    a.lm_part = p->pl;
-    a.lm_T = T_h;
-    a.logits = p->logits;
     a.cand_v = p->cand_v;
     a.cand_i = p->cand_i;
-    p->mk_grid = sms;
-    p->mk_stages = S;
-    p->mk_smem = smem;
+    p->ds_grid = sms;
+    p->ds_stages = S;
+    p->ds_smem = smem;
     p->persist = true;
     return true;
 }
@@ -902,18 +903,16 @@ static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t 
 // One tape step as a single cooperative launch (arrival counters cleared
 // first).
 static bool record_step_persist(CtxImpl *c, DecodePlan *p) {
-    MKArgs a = p->mk;
+    DSArgs a = p->ds;
     a.hist = p->hist;
     a.hist_rows = p->hist_rows;
-    if (!KLLM_CUDA(cudaMemsetAsync(p->d_done, 0, (p->phases.size() + 1) * sizeof(int),
-                                   c->stream)))
-        return false;
+    if (!KLLM_CUDA(cudaMemsetAsync(p->d_cnt, 0, p->cnt_n * sizeof(int), c->stream))) return false;
     auto kern = p->ti.hd == 32 ? k_decode_step<32>
                                : p->ti.hd == 64 ? k_decode_step<64> : k_decode_step<128>;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p->mk_grid);
-    cfg.blockDim = dim3(MK_THREADS);
-    cfg.dynamicSmemBytes = p->mk_smem;
+    cfg.gridDim = dim3(p->ds_grid);
+    cfg.blockDim = dim3(DS_THREADS);
+    cfg.dynamicSmemBytes = p->ds_smem;
     cfg.stream = c->stream;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeCooperative;

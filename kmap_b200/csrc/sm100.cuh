@@ -96,8 +96,40 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// Bulk copy with an L2 eviction hint (policy from l2_evict_first()).
+__device__ __forceinline__ void bulk_load_hint(void *dst, const void *src, uint32_t bytes,
+                                               uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy for data read once (streamed weights): evict first.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Ordered sum of T <= 8 chunk partials p[0], p[stride], ... written by
+// other CTAs: all loads are issued before the adds (a loop bounded by a
+// runtime T would wait one memory round trip per partial), then added in
+// chunk order -- the reference's reduction (_tape_runner.c:646-662).
+__device__ __forceinline__ float sum_parts(const float *p, size_t stride, int T) {
+    float v[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) v[t] = t < T ? __ldcg(p + t * stride) : 0.f;
+    float a = v[0];
+#pragma unroll
+    for (int t = 1; t < 8; t++)
+        if (t < T) a = __fadd_rn(a, v[t]);
+    return a;
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start

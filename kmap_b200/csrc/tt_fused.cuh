@@ -286,11 +286,7 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
         for (int c = threadIdx.x; c < BW; c += NC) {
             const int n = col0 + c;
             if (n >= a.F) continue;
-            float g = __ldcg(P + n), u = __ldcg(P + a.F + n);
-            for (int tt = 1; tt < T; tt++) {
-                g = __fadd_rn(g, __ldcg(P + (size_t)tt * a.N + n));
-                u = __fadd_rn(u, __ldcg(P + (size_t)tt * a.N + a.F + n));
-            }
+            const float g = sum_parts(P + n, a.N, T), u = sum_parts(P + a.F + n, a.N, T);
             const double d = (double)g;
             a.y[n] = __fmul_rn((float)(d / (1.0 + exp(-d))), u);
         }
@@ -300,8 +296,7 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
         for (int c = threadIdx.x; c < BN; c += NC) {
             const int n = col0 + c;
             if (n >= a.N) continue;
-            float v = __ldcg(P + n);
-            for (int tt = 1; tt < T; tt++) v = __fadd_rn(v, __ldcg(P + (size_t)tt * a.N + n));
+            const float v = sum_parts(P + n, a.N, T);
             if (a.emode == E_Y) {
                 a.y[n] = v;
             } else if (a.emode == E_RESID) {

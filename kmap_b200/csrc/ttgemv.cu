@@ -242,9 +242,7 @@ __global__ void k_tt_reduce(const float *__restrict__ part, int T, long long rn,
                             float *__restrict__ y) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rn;
          i += (long long)gridDim.x * blockDim.x) {
-        float acc = part[i];
-        for (int t = 1; t < T; t++) acc = __fadd_rn(acc, part[(size_t)t * rn + i]);
-        y[i] = acc;
+        y[i] = sum_parts(part + i, (size_t)rn, T);
     }
 }
 

@@ -80,3 +80,27 @@ def test_infer_bytes_matches_reference(gpu, ref, chip_dir):
         # a callback that asks to stop ends generation after that token
         out_s, gen_s, _ = chip.infer_bytes(text, 12, stop_after=3)
         assert gen_s == 3 and out_s == b"".join(pieces[:3])
+
+
+def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path):
+    """Two layers at the TinyLlama-1.1B widths (K = 2048 and 5632, N up to
+    32000, eight K-chunks per column): the fused step kernel's real tile,
+    ring and codebook-table geometry, against the compiled reference
+    runtime on the same chip."""
+    import kmap_b200
+    from kmap_b200 import chipgen
+    spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
+    spec.num_layers = 2
+    spec.max_seq = 256
+    path = chipgen.ensure_chip(str(tmp_path), spec)
+    prompt = np.random.default_rng(3).integers(3, spec.vocab_size, 6).astype(np.int32)
+    max_new = 6
+    h, info = ref.chip(path)
+    toks_r, lg_r = ref.greedy_logits(h, prompt, max_new, spec.vocab_size)
+    ref.L.refh_chip_destroy(h)
+    with kmap_b200.Chip(path) as chip:
+        toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
+        assert chip.stats()["fused"] == 1
+    assert toks_g.tolist() == toks_r.tolist()
+    n = len(prompt) + max_new - 1   # the last step's logits are not computed
+    np.testing.assert_allclose(lg_g[:n], lg_r[:n], rtol=RTOL, atol=ATOL)
