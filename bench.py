@@ -275,7 +275,8 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
     chip_path = config0_chip(rank)
-    chip = kmap_b200.Chip(chip_path)
+    order = kmap_b200.ORDER_FAST if args.order == "fast" else kmap_b200.ORDER_EXACT
+    chip = kmap_b200.Chip(chip_path, order=order)
     p = prompt_ids(seed=rank)
     t0 = time.time()
     chip.infer(p, GEN)      # first call prepares the plan (weights to HBM, graph)
@@ -362,6 +363,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--order", default="exact", choices=["exact", "fast"],
+                    help="TT-GEMV summation order of the decode step: the reference's "
+                         "chunked order (bit-identical MATMUL_TT) or the finer split")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling aid: decode on a TinyLlama-width chip with this many "
                          "layers (small enough for a profiler), print ms per tape step, "

@@ -56,13 +56,23 @@ enum {
     KLLM_MODE_FUSED = 2     /* fused plan or an error */
 };
 
+/* Summation order of the fused decode step's TT-GEMVs. */
+enum {
+    KLLM_ORDER_EXACT = 0,   /* the reference's chunked order: every MATMUL_TT
+                               result is bit-identical to _tape_runner.c's */
+    KLLM_ORDER_FAST = 1     /* K split finer across warps (decode only): same
+                               tokens and logits within the decode tolerance,
+                               more parallelism in the narrow projections */
+};
+
 typedef struct {
     int mode;                /* KLLM_MODE_* */
     float *logits_out;       /* optional host buffer: the logits row after
                                 every tape step, [logits_rows][vocab] */
     int logits_rows;         /* capacity of logits_out in rows */
     int use_graphs;          /* replay each step as a CUDA graph (fused) */
-    int reserved[8];
+    int order;               /* KLLM_ORDER_*, fused decode step */
+    int reserved[7];
 } kllm_infer_opts;
 
 typedef struct {

@@ -135,7 +135,7 @@ def require_gpu():
 
 class InferOpts(C.Structure):
     _fields_ = [("mode", C.c_int), ("logits_out", C.c_void_p), ("logits_rows", C.c_int),
-                ("use_graphs", C.c_int), ("reserved", C.c_int * 8)]
+                ("use_graphs", C.c_int), ("order", C.c_int), ("reserved", C.c_int * 7)]
 
 
 class InferStats(C.Structure):
@@ -145,6 +145,7 @@ class InferStats(C.Structure):
 
 
 MODE_AUTO, MODE_GENERIC, MODE_FUSED = 0, 1, 2
+ORDER_EXACT, ORDER_FAST = 0, 1
 
 
 def tt_gemv_host(x: np.ndarray, codebook: np.ndarray, idx: np.ndarray) -> np.ndarray:
@@ -173,8 +174,9 @@ INFO_KEYS = ("vocab_size", "hidden_dim", "num_layers", "num_kv_heads", "head_dim
 class Chip:
     """A chip directory loaded into a device tape context."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, order: int = 0):
         self.path = path
+        self.order = order        # ORDER_EXACT / ORDER_FAST for the fused decode step
         h = lib().kllm_chip_open(path.encode())
         if not h:
             msg = last_error()
@@ -206,11 +208,13 @@ class Chip:
     def __exit__(self, *a):
         self.close()
 
-    def set_opts(self, mode=MODE_AUTO, logits: np.ndarray | None = None, use_graphs=True):
+    def set_opts(self, mode=MODE_AUTO, logits: np.ndarray | None = None, use_graphs=True,
+                 order=None):
         o = InferOpts()
         lib().kllm_default_infer_opts(C.byref(o))
         o.mode = mode
         o.use_graphs = 1 if use_graphs else 0
+        o.order = self.order if order is None else order
         if logits is not None:
             assert logits.dtype == np.float32 and logits.flags.c_contiguous
             o.logits_out = logits.ctypes.data

@@ -51,9 +51,10 @@ struct DSPhase {
     TTXDesc d;                 // GEMV layout (ttx.cuh)
     int npieces;               // 16-step pieces per group
     int xs;                    // floats per chunk row of the staged x
+    unsigned lmagic;           // ceil(2^32 / L): r / L for equal chunks of L rows
     const uint8_t *stream;
-    const float *cb;           // raw codebook (copy 0 of the table)
-    int cb_bytes;              // n_codes * 4 rounded up to 16
+    const float *table;        // replicated codebook table (ttx.cuh), built at upload
+    int table_bytes;
     int xmode, emode;
     const float *x;            // DX_NORM: residual; DX_VEC: input vector
     const float *norm_w;
@@ -69,7 +70,7 @@ struct DSArgs {
     int *done;                 // [nphases] arrivals (zeroed per step)
     int *status;
     int *abort;
-    int stages, tab_cap, xc_cap;
+    int stages, tab_cap, wn_cap, xc_cap;
     // step state and embedding
     StepState *st;
     const float *embed;
@@ -100,7 +101,6 @@ constexpr int DS_MAX_STAGES = 32;
 constexpr int DS_PIECE_STEPS = 16;           // steps per ring stage (16 KB: one issuing
                                              // thread keeps HBM busy only with pieces this big)
 constexpr int DS_STAGE = DS_PIECE_STEPS * TTX_STEP;
-constexpr int DS_XU = 24;                    // x values per consumer thread in flight
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
@@ -121,6 +121,22 @@ __device__ __forceinline__ bool ds_wait_counter(const int *ctr, int target, int 
             return false;
         }
         __nanosleep(20);
+    }
+    return true;
+}
+
+// mbar_wait for the support warps (producer, table builder): their waits are
+// long, so they sleep between polls instead of taking issue slots from the
+// consumer warps on the same scheduler.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, int *status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            if (status) atomicOr(status, ST_WAIT_TIMEOUT);
+            return false;
+        }
+        __nanosleep(64);
     }
     return true;
 }
@@ -162,28 +178,18 @@ __device__ __forceinline__ int ds_token(const DSArgs &a) {
     return (tok < 0 || tok >= a.vocab) ? -1 : tok;
 }
 
-// Index k of x -> its slot in the staged, chunk-major x, for increasing k.
-struct DSSlot {
-    const TTXDesc &d;
-    int xs, t, start, end;
-    __device__ DSSlot(const TTXDesc &dd, int xss) : d(dd), xs(xss), t(0), start(0), end(dd.chunk_len(0)) {}
-    __device__ __forceinline__ int at(int k) {
-        while (k >= end && t + 1 < d.T) {
-            t++;
-            start = end;
-            end += d.chunk_len(t);
-        }
-        return t * xs + (k - start);
-    }
-};
-
 __device__ __forceinline__ uint32_t lo16(uint32_t w) { return w & 0xffffu; }
 __device__ __forceinline__ uint32_t hi16(uint32_t w) { return w >> 16; }
 
-// Slot -> table word for the two halves of a stream word.
+// Table word at a slot (a byte offset into the table).
+__device__ __forceinline__ float ds_tab(const float *tab, uint32_t off) {
+    return *reinterpret_cast<const float *>(reinterpret_cast<const char *>(tab) + off);
+}
+
+// The two columns' values for the low or high halves of two stream words.
 __device__ __forceinline__ float2 ds_gather(const float *tab, uint32_t w0, uint32_t w1, int hi) {
-    return hi ? make_float2(tab[hi16(w0)], tab[hi16(w1)])
-              : make_float2(tab[lo16(w0)], tab[lo16(w1)]);
+    return hi ? make_float2(ds_tab(tab, hi16(w0)), ds_tab(tab, hi16(w1)))
+              : make_float2(ds_tab(tab, lo16(w0)), ds_tab(tab, lo16(w1)));
 }
 
 // The 8 gathered (column 0, column 1) pairs of one step.
@@ -273,13 +279,15 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     __shared__ __align__(16) float pctx[NPG][HD];
     __shared__ int s_flag, s_tok;
     __shared__ int ri[DS_NCW];
+    __shared__ float2 sub_y[DS_NCW][4];        // split groups: each warp's column sums
 
     const int G = gridDim.x, cta = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.stages;
     uint8_t *ring = smem;
     float *tabs = reinterpret_cast<float *>(smem + (size_t)S * DS_STAGE);   // 2 tables
-    float *xc = tabs + 2 * a.tab_cap;  // staged x, chunk-major
+    float *wns = tabs + 2 * a.tab_cap; // 2 phases' norm weights
+    float *xc = wns + 2 * a.wn_cap;    // staged x, chunk-major
     float *sc = xc;                    // attention scores (no GEMV then)
     uint64_t *full = reinterpret_cast<uint64_t *>(xc + a.xc_cap);
     uint64_t *empty = full + S;
@@ -309,8 +317,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     // ================================================================ producer
     if (warp == DS_TABLER) {
         {
-            // The tables, two phases deep: the codebook by bulk copy into
-            // copy 0, copies 1..R-1 by the warp's lanes.
+            // The tables, two phases deep, by bulk copy of the replicated
+            // table built at upload.
             int q = 0;
             for (int p = 0; p < a.nphases; p++) {
                 const DSPhase &ph = a.phases[p];
@@ -318,26 +326,26 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 if (ld_acquire(a.abort)) return;
                 const int slot = q & 1;
                 float *tab = tabs + slot * a.tab_cap;
-                if (q >= 2 && !mbar_wait(&tfree[slot], ((q >> 1) - 1) & 1, a.status)) {
+                if (q >= 2 && !mbar_wait_idle(&tfree[slot], ((q >> 1) - 1) & 1, a.status)) {
                     atomicExch(a.abort, 1);
                     return;
                 }
-                if (lane == 0) {
-                    const uint32_t cb = (uint32_t)ph.cb_bytes;
-                    mbar_expect_tx(rawfull, cb);
+                if (lane == 0) {   // the table, and the norm weights the prologue reads
+                    const uint32_t cb = (uint32_t)ph.table_bytes;
+                    const uint32_t wb = ph.xmode != DX_VEC ? (uint32_t)ph.d.K * 4 : 0u;
+                    mbar_expect_tx(rawfull, cb + wb);
                     for (uint32_t off = 0; off < cb; off += 32768)
                         bulk_load(reinterpret_cast<uint8_t *>(tab) + off,
-                                  reinterpret_cast<const uint8_t *>(ph.cb) + off,
+                                  reinterpret_cast<const uint8_t *>(ph.table) + off,
                                   min(32768u, cb - off), rawfull);
+                    for (uint32_t off = 0; off < wb; off += 32768)
+                        bulk_load(reinterpret_cast<uint8_t *>(wns + slot * a.wn_cap) + off,
+                                  reinterpret_cast<const uint8_t *>(ph.norm_w) + off,
+                                  min(32768u, wb - off), rawfull);
                 }
-                if (!mbar_wait(rawfull, q & 1, a.status)) {
+                if (!mbar_wait_idle(rawfull, q & 1, a.status)) {
                     atomicExch(a.abort, 1);
                     return;
-                }
-                const int npad = ph.d.npad, R = ph.d.R;
-                for (int e = lane; e < npad; e += 32) {
-                    const float v = tab[e];
-                    for (int c = 1; c < R; c++) tab[c * npad + ttx_swz(e, c)] = v;
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tready[slot]);
@@ -354,22 +362,23 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             const DSPhase &ph = a.phases[p];
             if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
             if (ld_acquire(a.abort)) return;
-            const int M = (ph.ntasks - cta + G - 1) / G, ns = ph.d.ns, np = ph.npieces;
-            for (int r = 0; DS_NCW * r < M; r++) {
-                const int nr = min(DS_NCW, M - DS_NCW * r);
+            const int W = ph.d.W;
+            const int J = (ph.ntasks - cta + G - 1) / G * W, ns = ph.d.ns, np = ph.npieces;
+            for (int r = 0; DS_NCW * r < J; r++) {
+                const int nr = min(DS_NCW, J - DS_NCW * r);
                 for (int b = 0; b < np; b++) {
                     const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
-                    for (int m = DS_NCW * r; m < DS_NCW * r + nr; m++, seq++) {
-                        const int g = cta + m * G;
+                    for (int j = DS_NCW * r; j < DS_NCW * r + nr; j++, seq++) {
+                        const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
                         const int s = seq % S;
-                        if (seq >= S && !mbar_wait(&empty[s], ((seq / S) - 1) & 1, a.status)) {
+                        if (seq >= S && !mbar_wait_idle(&empty[s], ((seq / S) - 1) & 1, a.status)) {
                             atomicExch(a.abort, 1);
                             return;
                         }
                         stage_seq[s] = seq;
                         mbar_expect_tx(&full[s], bytes);
                         bulk_load_hint(ring + (size_t)s * DS_STAGE,
-                                       ph.stream + ((size_t)g * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
+                                       ph.stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
                                        bytes, &full[s], pol);
                     }
                 }
@@ -412,65 +421,91 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 cbar_sync();
                 src = a.embed + (size_t)s_tok * K;
             }
-            // all of x (and the norm weights) in flight at once, then
-            // rmsnorm from registers: x * rsqrt(mean(x^2) + eps) * w
+            // Warp w stages its rows of x -- chunk w (reference order,
+            // T <= 8) or chunks W*w .. W*w + W - 1 (fast order: equal chunks
+            // of L rows, one contiguous range) -- then rmsnorm in place:
+            // x * rsqrt(mean(x^2) + eps) * w.  Compact loops: this runs once
+            // per phase and must not crowd the task loop out of the
+            // instruction cache.
             const bool norm = xmode != DX_VEC;
+            const int CH = (d.T + DS_NCW - 1) / DS_NCW;   // chunks per warp
+            const int wrows = CH == 1 ? (warp < d.T ? d.chunk_len(warp) : 0) : CH * d.base;
+            const int wk0 = CH == 1 ? (warp < d.T ? d.chunk_start(warp) : 0) : warp * CH * d.base;
+            // row r of the warp's range -> its slot in xc
+            auto slot_of = [&](int r) {
+                const int cq = CH == 1 ? 0 : (int)__umulhi((unsigned)r, ph.lmagic);
+                return (CH * warp + cq) * xs + (r - cq * d.base);
+            };
             float ss = 0.f;
-            float v[DS_XU], w[DS_XU];
-            const bool one = K <= DS_XU * DS_NC;
-            for (int kb = 0; kb < K; kb += DS_XU * DS_NC) {
+            for (int r0 = lane; r0 < wrows; r0 += 8 * 32) {
+                float v[8];
 #pragma unroll
-                for (int u = 0; u < DS_XU; u++) {
-                    const int k = kb + tid + u * DS_NC;
-                    v[u] = k < K ? __ldcg(src + k) : 0.f;
-                    w[u] = (norm && k < K) ? __ldg(ph.norm_w + k) : 0.f;
-                }
+                for (int u = 0; u < 8; u++)
+                    v[u] = r0 + 32 * u < wrows ? __ldcg(src + wk0 + r0 + 32 * u) : 0.f;
 #pragma unroll
-                for (int u = 0; u < DS_XU; u++) ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
-                if (!one || !norm) {   // stage x as is (scaled below when K is long)
-                    DSSlot sl(d, xs);
-#pragma unroll
-                    for (int u = 0; u < DS_XU; u++) {
-                        const int k = kb + tid + u * DS_NC;
-                        if (k < K) xc[sl.at(k)] = v[u];
+                for (int u = 0; u < 8; u++)
+                    if (r0 + 32 * u < wrows) {
+                        xc[slot_of(r0 + 32 * u)] = v[u];
+                        ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
                     }
-                }
             }
-            if (norm) {
-                const float tot = ds_block_sum(ss, red);
-                const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)K), ph.eps);
-                const float rsq = (float)(1.0 / sqrt((double)add));
-                DSSlot sl(d, xs);
-                if (one) {
-#pragma unroll
-                    for (int u = 0; u < DS_XU; u++) {
-                        const int k = tid + u * DS_NC;
-                        if (k < K) xc[sl.at(k)] = __fmul_rn(__fmul_rn(v[u], rsq), w[u]);
-                    }
-                } else {
-                    for (int k = tid; k < K; k += DS_NC) {
-                        const int o = sl.at(k);
-                        xc[o] = __fmul_rn(__fmul_rn(xc[o], rsq), __ldg(ph.norm_w + k));
-                    }
-                }
-            }
-            cbar_sync();
             const int slot = q & 1;
             const float *tab = tabs + slot * a.tab_cap;
             bad = !mbar_wait(&tready[slot], (q >> 1) & 1, a.status);
             if (bad) atomicExch(a.abort, 1);
+            if (norm) {
+                const float *wn = wns + slot * a.wn_cap;   // staged with the table
+                const float tot = ds_block_sum(ss, red);
+                const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)K), ph.eps);
+                const float rsq = (float)(1.0 / sqrt((double)add));
+                for (int r = lane; r < wrows; r += 32) {
+                    const int o = slot_of(r);
+                    xc[o] = __fmul_rn(__fmul_rn(xc[o], rsq), wn[wk0 + r]);
+                }
+            }
+            cbar_sync();
             // ------------------------------------------------ tasks
-            const int M = (ph.ntasks - cta + G - 1) / G, ns = d.ns, np = ph.npieces;
-            const int len = d.chunk_len(t);
+            const int W = d.W;
+            const int J = (ph.ntasks - cta + G - 1) / G * W, ns = d.ns, np = ph.npieces;
             const int nfull = d.base / 8;             // steps inside every chunk
-            const float *xr = t < d.T ? xc + t * xs : xc;
             const int pos = a.st->pos;
-            for (int m = warp; m < M; m += DS_NCW) {
-                const int r = m / DS_NCW, nr = min(DS_NCW, M - DS_NCW * r);
+            // warp task j: sub-task w = j % W of group m = j / W; a group's W
+            // sub-tasks sit on W adjacent warps of one round
+            for (int j = warp; j < J; j += DS_NCW) {
+                const int r = j / DS_NCW, nr = min(DS_NCW, J - DS_NCW * r);
+                const int m = j / W, w = j % W;
                 const int g = cta + m * G;
+                const int ch = DS_NCW * w + t;        // this lane's chunk
+                const int len = d.chunk_len(ch);
+                const float *xr = ch < d.T ? xc + ch * xs : xc;
+                const int nch = min(DS_NCW, d.T - DS_NCW * w);   // chunks in this sub-task
+                const int n0 = ttx_col(d, g, 2 * cp), n1 = ttx_col(d, g, 2 * cp + 1);
+                // the epilogue's operands, fetched while the task computes
+                float2 ea = make_float2(0.f, 0.f), eb = make_float2(0.f, 0.f);
+                if (t == 0 && w == 0) {
+                    if (ph.emode == DE_RESID) {
+                        const float *h = ph.hold;
+                        if (!h) {
+                            const int tok = ds_token(a);
+                            h = a.embed + (size_t)(tok < 0 ? 0 : tok) * a.H;
+                        }
+                        ea.x = n0 >= 0 ? __ldcg(h + n0) : 0.f;
+                        ea.y = n1 >= 0 ? __ldcg(h + n1) : 0.f;
+                    } else if (ph.emode == DE_QKV && g < d.rope_heads * (HD / 8) && pos < a.max_pos) {
+                        const float *cr = a.rope_cos + (size_t)pos * HD, *sr = a.rope_sin + (size_t)pos * HD;
+                        if (n0 >= 0) {
+                            ea.x = __ldg(cr + n0 % HD);
+                            eb.x = __ldg(sr + n0 % HD);
+                        }
+                        if (n1 >= 0) {
+                            ea.y = __ldg(cr + n1 % HD);
+                            eb.y = __ldg(sr + n1 % HD);
+                        }
+                    }
+                }
                 float2 acc = make_float2(0.f, 0.f);
                 for (int b = 0; b < np; b++) {
-                    const int seq = seq_base + r * DS_NCW * np + b * nr + (m - DS_NCW * r);
+                    const int seq = seq_base + r * DS_NCW * np + b * nr + (j - DS_NCW * r);
                     const int s = seq % S;
                     if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status) ||
                                  !mbar_wait(&full[s], (seq / S) & 1, a.status))) {
@@ -493,13 +528,21 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 float2 y;
                 y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
                 y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
-                for (int tt = 1; tt < d.T; tt++) {
+                for (int tt = 1; tt < nch; tt++) {
                     float2 o;
                     o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
                     o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
                     y = __fadd2_rn(y, o);
                 }
-                const int n0 = ttx_col(d, g, 2 * cp), n1 = ttx_col(d, g, 2 * cp + 1);
+                if (W > 1) {   // sub-task sums of the group, in w order
+                    const int bar_id = 2 + warp / W;
+                    if (t == 0) sub_y[warp][cp] = y;
+                    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(32 * W) : "memory");
+                    if (w == 0)
+                        for (int ww = 1; ww < W; ww++) y = __fadd2_rn(y, sub_y[warp + ww][cp]);
+                    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(32 * W) : "memory");
+                    if (w != 0) continue;   // the group's first warp stores the result
+                }
                 if (ph.emode == DE_QKV) {
                     float2 pr;   // rotate-half partner (pair cp ^ 2)
                     pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
@@ -507,6 +550,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     if (t == 0 && !bad && pos < a.max_pos) {
                         const bool rot = g < d.rope_heads * (HD / 8);
                         const float yy[2] = {y.x, y.y}, pp[2] = {pr.x, pr.y};
+                        const float cc[2] = {ea.x, ea.y}, sn2[2] = {eb.x, eb.y};
                         const int nn[2] = {n0, n1};
 #pragma unroll
                         for (int k = 0; k < 2; k++) {
@@ -515,9 +559,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                             if (rot) {
                                 const int head = n / HD, dim = n % HD;
                                 const float rt = cp < 2 ? -pp[k] : pp[k];
-                                const float c = __ldg(a.rope_cos + (size_t)pos * HD + dim);
-                                const float sn = __ldg(a.rope_sin + (size_t)pos * HD + dim);
-                                const float v = __fadd_rn(__fmul_rn(yy[k], c), __fmul_rn(rt, sn));
+                                const float v = __fadd_rn(__fmul_rn(yy[k], cc[k]), __fmul_rn(rt, sn2[k]));
                                 if (head < a.nh)
                                     a.q[n] = v;
                                 else
@@ -530,21 +572,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     }
                 } else if (ph.emode == DE_RESID) {
                     if (t == 0 && !bad) {
-                        const float yy[2] = {y.x, y.y};
-                        const int nn[2] = {n0, n1};
-                        int tok = 0;
-                        if (!ph.hold) {
-                            tok = ds_token(a);
-                            tok = tok < 0 ? 0 : tok;
-                        }
-#pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const int n = nn[k];
-                            if (n < 0) continue;
-                            const float h0 = ph.hold ? __ldcg(ph.hold + n)
-                                                     : __ldg(a.embed + (size_t)tok * a.H + n);
-                            ph.out[n] = __fadd_rn(h0, yy[k]);
-                        }
+                        if (n0 >= 0) ph.out[n0] = __fadd_rn(ea.x, y.x);
+                        if (n1 >= 0) ph.out[n1] = __fadd_rn(ea.y, y.y);
                     }
                 } else if (ph.emode == DE_SWIGLU) {
                     float2 up;
@@ -578,7 +607,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     }
                 }
             }
-            seq_base += M * np;
+            seq_base += J * np;
             cbar_sync();   // every warp's outputs are stored and the table is free
             if (tid == 0) mbar_arrive(&tfree[slot]);
             q++;

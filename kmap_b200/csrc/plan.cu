@@ -486,6 +486,7 @@ struct DecodePlan {
     float *graph_hist = nullptr;   // history buffer baked into the graph
     // persistent step kernel
     bool persist = false;
+    int order = 0;                 // KLLM_ORDER_* the layouts were built for
     int ds_grid = 0, ds_stages = 0;
     size_t ds_smem = 0;
     DSArgs ds = {};
@@ -569,6 +570,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     const int max_table = 48 * 1024;
     std::vector<TTXDesc> desc(nmat);
     std::vector<uint8_t *> streams(nmat);
+    std::vector<float *> tables(nmat);
     std::vector<int> xsz(nmat);
     int tab_cap = 0, xc_cap = (p->max_pos + 3) & ~3;
     auto own = [&](void *b) { p->ds_bufs.push_back(b); };
@@ -577,13 +579,24 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         const DevSlot &w = c->ds[tts[i]];
         const int role = i + 1 == nmat ? 4 : i % 4;   // 0 qkv 1 o 2 gate_up 3 down 4 lm_head
         const int mode = role == 0 ? TTX_ROPE : role == 2 ? TTX_GATE_UP : TTX_IDENT;
-        if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, hd, t.nh + nkv, max_table, max_r,
+        // fast order: split a group over W warps while the phase still fits
+        // one round of warp tasks (decode tolerance instead of bit-exact sums)
+        int W = 1;
+        if (p->order == KLLM_ORDER_FAST) {
+            const int ng = mode == TTX_GATE_UP ? (sl.tt_N / 2 + 3) / 4 : (sl.tt_N + 7) / 8;
+            while (W < 8 && (long long)ng * 2 * W <= (long long)sms * DS_NCW &&
+                   sl.tt_K % (16 * 8 * W) == 0)
+                W *= 2;
+        }
+        if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, hd, t.nh + nkv, max_table, max_r, W,
                           &desc[i]))
             return false;
         const TTXDesc &d = desc[i];
         if (!KLLM_CUDA(cudaMalloc((void **)&streams[i], d.stream_bytes()))) return false;
         own(streams[i]);
-        if (!ttx_build(c->stream, w.d_idx, w.d_cb, d, streams[i], nullptr)) return false;
+        if (!KLLM_CUDA(cudaMalloc((void **)&tables[i], d.table_elems() * 4))) return false;
+        own(tables[i]);
+        if (!ttx_build(c->stream, w.d_idx, w.d_cb, d, streams[i], tables[i])) return false;
         tab_cap = std::max(tab_cap, (int)d.table_elems());
         // staged x: chunk rows of 8 * ns floats, padded to 4 mod 32 floats so
         // that the 8 chunks' float4 reads fall in different banks
@@ -592,10 +605,12 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         xc_cap = std::max(xc_cap, d.T * xsz[i]);
     }
     if (!KLLM_CUDA(cudaStreamSynchronize(c->stream))) return false;
-    // shared memory: ring | 2 tables | staged x (attention scores alias
-    // it) | mbarriers
+    // shared memory: ring | 2 tables | 2 norm weight vectors | staged x
+    // (attention scores alias it) | mbarriers
+    if (H % 4) return false;   // norm weights arrive by bulk copy
     xc_cap = (xc_cap + 3) & ~3;
-    const size_t fixed = (size_t)4 * (2 * tab_cap + xc_cap) + 8 * 5 + 16;
+    const int wn_cap = (H + 3) & ~3;
+    const size_t fixed = (size_t)4 * (2 * tab_cap + 2 * wn_cap + xc_cap) + 8 * 5 + 16;
     if (avail <= fixed + 2 * ((size_t)DS_STAGE + 16)) return false;
     const int S = (int)std::min<size_t>(DS_MAX_STAGES, (avail - fixed) / (DS_STAGE + 20));
     const size_t smem = (size_t)S * DS_STAGE + fixed + (size_t)8 * (2 * S) + (size_t)4 * S;
@@ -631,9 +646,10 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         m.d = d;
         m.npieces = (d.ns + DS_PIECE_STEPS - 1) / DS_PIECE_STEPS;
         m.xs = xsz[mi];
+        m.lmagic = (unsigned)((((unsigned long long)1 << 32) + d.base - 1) / d.base);
         m.stream = streams[mi];
-        m.cb = c->ds[tts[mi]].d_cb;
-        m.cb_bytes = ((d.n_codes + 3) & ~3) * 4;
+        m.table = tables[mi];
+        m.table_bytes = (int)(d.table_elems() * 4);
         m.xmode = xmode;
         m.emode = emode;
         m.x = x;
@@ -689,6 +705,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.abort = p->d_abort;
     a.stages = S;
     a.tab_cap = tab_cap;
+    a.wn_cap = wn_cap;
     a.xc_cap = xc_cap;
     a.st = p->st;
     a.embed = p->embed;
@@ -730,7 +747,7 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     DecodePlan *old = c->plan;
     if (old && old->max_pos >= max_pos && old->src_embed == d.embed &&
         old->src_cos == d.rope_cos && old->src_sin == d.rope_sin && old->ti.H == d.hidden &&
-        old->ti.V == d.vocab) {
+        old->ti.V == d.vocab && old->order == c->opts.order) {
         return true;   // reuse (weights are re-checked by upload_tt below)
     }
     TemplateInfo ti;
@@ -760,6 +777,7 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     plan_destroy(c);
     DecodePlan *p = new DecodePlan();
     p->ti = ti;
+    p->order = c->opts.order;
     p->max_pos = max_pos;
     p->src_embed = d.embed;
     p->src_cos = d.rope_cos;

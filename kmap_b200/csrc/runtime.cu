@@ -451,6 +451,11 @@ int kllm_set_infer_opts(TapeCtx *ctx, const kllm_infer_opts *o) {
         set_error("kllm_set_infer_opts: NULL argument");
         return -1;
     }
+    if (o->order != KLLM_ORDER_EXACT && o->order != KLLM_ORDER_FAST) {
+        set_error("kllm_set_infer_opts: order %d is not KLLM_ORDER_EXACT or KLLM_ORDER_FAST",
+                  o->order);
+        return -1;
+    }
     impl(ctx)->opts = *o;
     return 0;
 }

@@ -106,6 +106,12 @@ __device__ __forceinline__ void bulk_load_hint(void *dst, const void *src, uint3
         : "memory");
 }
 
+// Bring a line into L2 ahead of its use, kept there in preference to
+// streamed data.
+__device__ __forceinline__ void prefetch_l2_keep(const void *p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
 // L2 policy for data read once (streamed weights): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first() {
     uint64_t p;

@@ -5,14 +5,16 @@
 namespace kllm {
 
 bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads,
-                  int max_table_bytes, int max_r, TTXDesc *d) {
+                  int max_table_bytes, int max_r, int split_w, TTXDesc *d) {
     if (K <= 0 || N <= 0 || n_codes <= 0) return false;
+    if (split_w != 1 && split_w != 2 && split_w != 4 && split_w != 8) return false;
     TTXDesc t = {};
     t.K = K;
     t.N = N;
     t.n_codes = n_codes;
-    t.T = tt_chunks(K);
-    if (t.T > 8) return false;
+    t.W = split_w;
+    t.T = split_w == 1 ? tt_chunks(K) : 8 * split_w;
+    if ((split_w == 1 && t.T > 8) || t.T > K) return false;
     t.base = K / t.T;
     t.rem = K % t.T;
     const int len_max = t.base + (t.rem > 0 ? 1 : 0);
@@ -32,19 +34,20 @@ bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads
         t.ngroups = (N + TTX_GCOLS - 1) / TTX_GCOLS;
     }
     t.npad = (n_codes + 31) & ~31;
+    // slots are byte offsets into the table: R * npad * 4 must fit 16 bits
     int r = 4;
     while (r > max_r || (r > 1 && ((size_t)r * t.npad * 4 > (size_t)max_table_bytes ||
-                                   (size_t)r * t.npad > 65536)))
+                                   (size_t)r * t.npad * 4 > 65536)))
         r >>= 1;
-    if ((size_t)t.npad * 4 > (size_t)max_table_bytes || t.npad > 65536) return false;
+    if ((size_t)t.npad * 4 > (size_t)max_table_bytes || (size_t)t.npad * 4 > 65536) return false;
     t.R = r;
     *d = t;
     return true;
 }
 
-// One thread per warp-wide gather of the decode kernel: group g, step s,
-// column half k, row e -- lane l = 8 * pair + chunk reads column
-// 2 * pair + k, row 8s + e of its chunk.  It chooses a codebook copy for
+// One thread per warp-wide gather of the decode kernel: group g, sub-task w,
+// step s, column half k, row e -- lane l = 8 * pair + c reads column
+// 2 * pair + k, row 8s + e of chunk 8w + c.  It chooses a codebook copy for
 // every distinct code so that the bank holding the most distinct words holds
 // as few as possible.  Exact: for cap = 1, 2, ... every code is inserted with
 // a breadth-first augmenting path over banks (a bank may hold cap words).
@@ -55,14 +58,15 @@ __global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
     const int e = (int)(gid & 7), k = (int)((gid >> 3) & 1);
     const long long gs = gid >> 4;
     const int s = (int)(gs % d.ns);
-    const int g = (int)(gs / d.ns);
+    const long long gw = gs / d.ns;          // g * W + w
+    const int g = (int)(gw / d.W), w = (int)(gw % d.W);
 
     int code[32];   // distinct codes
     int lane_u[32];
     int nu = 0;
     for (int l = 0; l < 32; l++) {
         lane_u[l] = -1;
-        const int t = l & 7, pair = l >> 3;
+        const int t = 8 * w + (l & 7), pair = l >> 3;
         const int row = 8 * s + e;
         if (row >= d.chunk_len(t)) continue;
         const int n = ttx_col(d, g, 2 * pair + k);
@@ -132,13 +136,13 @@ __global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
     for (int l = 0; l < 32; l++)
         if (lane_u[l] >= 0) {
             const int u = lane_u[l];
-            fill = copy[u] * d.npad + ttx_swz(code[u], copy[u]);
+            fill = 4 * (copy[u] * d.npad + ttx_swz(code[u], copy[u]));
             break;
         }
-    uint16_t *step = reinterpret_cast<uint16_t *>(out + ((size_t)g * d.ns + s) * TTX_STEP);
+    uint16_t *step = reinterpret_cast<uint16_t *>(out + ((size_t)gw * d.ns + s) * TTX_STEP);
     for (int l = 0; l < 32; l++) {
         const int u = lane_u[l];
-        const int slot = u >= 0 ? copy[u] * d.npad + ttx_swz(code[u], copy[u]) : fill;
+        const int slot = u >= 0 ? 4 * (copy[u] * d.npad + ttx_swz(code[u], copy[u])) : fill;
         step[k * 256 + l * 8 + e] = (uint16_t)slot;
     }
 }
@@ -153,7 +157,7 @@ __global__ void k_ttx_table(const float *__restrict__ cb, const TTXDesc d, float
 
 bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDesc &d,
                uint8_t *stream, float *table) {
-    const long long ngather = (long long)d.ngroups * d.ns * 16;
+    const long long ngather = (long long)d.ngroups * d.W * d.ns * 16;
     if (ngather <= 0) return false;
     const int bs = 128;
     k_ttx_build<<<(unsigned)((ngather + bs - 1) / bs), bs, 0, s>>>(idx, d, stream, ngather);

@@ -15,12 +15,18 @@
 //    each lane reads a step with two conflict-free 128-bit loads.
 //  * Bank-spread codebook.  The codebook is stored R times (R <= 4) in a
 //    table of R x npad floats; copy r keeps entry e at row e >> 5 of the
-//    copy, bank (e & 31) ^ h(e >> 5, r).  The stream holds table slots, not
+//    copy, bank (e & 31) ^ h(e >> 5, r).  The stream holds table slots (the
+//    byte offset of the chosen copy's word, so R * npad * 4 <= 64 KB), not
 //    codes: for every warp-wide gather (one row, one column of each lane)
 //    the upload picks the copy of each code so that the most-loaded bank
 //    holds as few distinct words as possible (an exact bipartite
 //    assignment with bank capacities).  The values read are the codebook
 //    entries themselves, so products and sums are unchanged bit for bit.
+//  * Split groups (decode's fast order).  With W > 1 a group's K is cut into
+//    8W equal chunks instead of the reference's T: sub-task w of the group
+//    (its own NS steps, lane chunk 8w + lane % 8) goes to its own warp, and
+//    the W partial sums are added in w order.  Same bytes, W times the
+//    warps; the sums are no longer the reference's bit for bit.
 //  * Column groups.  Plain matrices take 8 consecutive columns.  gate_up
 //    (N = 2F) takes gate columns 4g..4g+3 and the matching up columns, so a
 //    group holds both inputs of its SwiGLU.  QKV with RoPE takes, inside one
@@ -39,7 +45,8 @@ enum TTXCols : int { TTX_IDENT = 0, TTX_GATE_UP = 1, TTX_ROPE = 2 };
 
 struct TTXDesc {
     int K, N, n_codes;
-    int T, base, rem;     // the reference's chunking of K
+    int T, base, rem;     // the chunking of K (the reference's when W == 1)
+    int W;                // sub-tasks (warps) per group
     int ns;               // steps per group (8 rows of every chunk per step)
     int ngroups;
     int R, npad;          // codebook copies, entries per copy (multiple of 32)
@@ -47,7 +54,7 @@ struct TTXDesc {
     int F;                // TTX_GATE_UP: N == 2F
     int hd, rope_heads;   // TTX_ROPE: head dim, q + k heads (rotated)
     __host__ __device__ size_t stream_bytes() const {
-        return (size_t)ngroups * ns * TTX_STEP;
+        return (size_t)ngroups * W * ns * TTX_STEP;
     }
     __host__ __device__ size_t table_elems() const { return (size_t)R * npad; }
     __host__ __device__ int chunk_start(int t) const { return t * base + (t < rem ? t : rem); }
@@ -87,9 +94,10 @@ __host__ __device__ inline int ttx_col(const TTXDesc &d, int g, int c) {
 // Fill in the layout of a K x N matrix with n_codes codes.  R is the largest
 // of 4, 2, 1 (at most max_r) whose table fits max_table_bytes and whose
 // slots fit 16 bits.  TTX_ROPE needs hd (a multiple of 8) and the number
-// of rotated heads.
+// of rotated heads.  split_w = 1 keeps the reference's chunks; 2, 4 or 8
+// splits each group into that many sub-tasks (fast order).
 bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads,
-                  int max_table_bytes, int max_r, TTXDesc *d);
+                  int max_table_bytes, int max_r, int split_w, TTXDesc *d);
 // Build the slot stream and (table != nullptr) the replicated table on the
 // device.
 bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDesc &d,

@@ -21,11 +21,12 @@ def _oracle_run(oracle, path, prompt, max_new):
 
 
 @pytest.mark.parametrize("name", ["gqa", "mha", "tl"])
-@pytest.mark.parametrize("mode", ["generic", "auto"])
+@pytest.mark.parametrize("mode", ["generic", "auto", "auto-fast"])
 def test_tiny_chip_tokens_and_logits(gpu, oracle, chip_dir, name, mode):
     import kmap_b200
     path = chip_dir(name)
-    with kmap_b200.Chip(path) as chip:
+    order = kmap_b200.ORDER_FAST if mode == "auto-fast" else kmap_b200.ORDER_EXACT
+    with kmap_b200.Chip(path, order=order) as chip:
         V = chip.info["vocab_size"]
         prompt = np.random.default_rng(11).integers(3, V, 7)
         max_new = 20
@@ -82,7 +83,8 @@ def test_infer_bytes_matches_reference(gpu, ref, chip_dir):
         assert gen_s == 3 and out_s == b"".join(pieces[:3])
 
 
-def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path):
+@pytest.mark.parametrize("order", ["exact", "fast"])
+def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path, order):
     """Two layers at the TinyLlama-1.1B widths (K = 2048 and 5632, N up to
     32000, eight K-chunks per column): the fused step kernel's real tile,
     ring and codebook-table geometry, against the compiled reference
@@ -98,7 +100,8 @@ def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path):
     h, info = ref.chip(path)
     toks_r, lg_r = ref.greedy_logits(h, prompt, max_new, spec.vocab_size)
     ref.L.refh_chip_destroy(h)
-    with kmap_b200.Chip(path) as chip:
+    o = kmap_b200.ORDER_FAST if order == "fast" else kmap_b200.ORDER_EXACT
+    with kmap_b200.Chip(path, order=o) as chip:
         toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
         assert chip.stats()["fused"] == 1
     assert toks_g.tolist() == toks_r.tolist()
