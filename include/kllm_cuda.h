@@ -99,6 +99,33 @@ int kllm_plan_match(TapeCtx *ctx, int vocab_size, int hidden_dim, int head_dim,
                     const int *kv_in_slots, const int *kv_out_slots, int logits_slot,
                     int n_layers, int num_kv_heads, char *why, int why_len);
 
+/* Build the fused decode plan now (weights to the device layout, buffers)
+ * for contexts of up to max_pos positions, instead of at the first
+ * processor_infer call.  Same model arguments as processor_infer.  0 on
+ * success, -1 (kllm_last_error) when the tape does not match the template. */
+int kllm_plan_prepare(TapeCtx *ctx, const float *embed_table, int vocab_size, int hidden_dim,
+                      const float *rope_cos, const float *rope_sin, int head_dim,
+                      int token_embed_slot, int rope_cos_slot, int rope_sin_slot,
+                      const int *kv_in_slots, const int *kv_out_slots, int logits_slot,
+                      int n_layers, int num_kv_heads, int max_pos);
+
+/* ----------------------------------------------- column-sharded decode -----
+ * One process per GPU.  Rank r of `world` stores and multiplies every
+ * world-th column group of each TT matrix (N is sharded, K and the
+ * codebooks are not), and stores its results into every rank's copy of the
+ * activations over NVLink peer memory inside the decode kernel; each output
+ * column's arithmetic is unchanged, so results equal the 1-GPU run.
+ * Sequence: kllm_shard_set (before the plan exists), kllm_plan_prepare,
+ * kllm_shard_export on every rank, exchange the blocks (any transport,
+ * e.g. torch.distributed), kllm_shard_connect with all blocks in rank
+ * order, then processor_infer on every rank with the same arguments.  The
+ * reference has no multi-GPU path. */
+int kllm_shard_set(TapeCtx *ctx, int rank, int world);
+/* This rank's block (CUDA IPC handles); *len gets its size. */
+int kllm_shard_export(TapeCtx *ctx, void *out, size_t cap, size_t *len);
+/* world blocks of per_rank bytes each, in rank order. */
+int kllm_shard_connect(TapeCtx *ctx, const void *all, size_t per_rank);
+
 /* ----------------------------------------------------------- TT-GEMV -----
  * y[r][n] = sum_k fl(x[r][k] * codebook[idx[k][n]]) in the accumulation
  * order of the reference TT-GEMV (_tape_runner.c:495-663): K is cut into
@@ -158,6 +185,9 @@ int kllm_chip_info(kllm_chip *chip, int *info);
  * csrc/kllm.c:566-584, minus the BPE). */
 int kllm_chip_infer(kllm_chip *chip, const int *prompt, int prompt_len, int max_new,
                     int eos_token_id, int *out_tokens, int *out_len);
+
+/* kllm_plan_prepare with the chip's tables, for its max_seq_len. */
+int kllm_chip_plan_prepare(kllm_chip *chip);
 
 /* processor_infer_bytes with the chip's ROMs, as `kllm infer` calls it
  * (csrc/kllm.c:566-584); max_seq_tokens <= 0 means the chip's max_seq_len. */

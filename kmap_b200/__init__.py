@@ -44,6 +44,11 @@ _SIGS = {
                                      C.c_int, C.c_int, C.c_void_p]),
     "kllm_chip_open": (C.c_void_p, [C.c_char_p]),
     "kllm_chip_close": (None, [C.c_void_p]),
+    "kllm_chip_plan_prepare": (C.c_int, [C.c_void_p]),
+    "kllm_shard_set": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "kllm_shard_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t,
+                                    C.POINTER(C.c_size_t)]),
+    "kllm_shard_connect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     "kllm_chip_ctx": (C.c_void_p, [C.c_void_p]),
     "kllm_chip_info": (C.c_int, [C.c_void_p, _fp(C.c_int)]),
     "kllm_chip_infer": (C.c_int, [C.c_void_p, _fp(C.c_int), C.c_int, C.c_int, C.c_int,
@@ -145,6 +150,16 @@ class InferStats(C.Structure):
 
 
 MODE_AUTO, MODE_GENERIC, MODE_FUSED = 0, 1, 2
+
+
+def exchange_blocks(block: bytes, group=None) -> list:
+    """All ranks' shard blocks, in rank order, over torch.distributed (any
+    backend: the blocks are a few hundred bytes of host data)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, block, group=group)
+    return out
+
 ORDER_EXACT, ORDER_FAST = 0, 1
 
 
@@ -239,6 +254,37 @@ class Chip:
                                   _iptr(ki), _iptr(ko), i["logits_slot"], i["num_layers"],
                                   i["num_kv_heads"], why, 512)
         return r == 1, why.value.decode()
+
+    # ------------------------------------------------ column-sharded decode
+    def shard(self, rank: int, world: int) -> bytes:
+        """Make this chip rank `rank` of a `world`-GPU column-sharded decode:
+        build its plan (this rank's column groups only) and return the block
+        every other rank needs (pass all blocks, in rank order, to connect)."""
+        check(lib().kllm_shard_set(self.ctx, rank, world), "kllm_shard_set")
+        self.set_opts()
+        check(lib().kllm_chip_plan_prepare(self.h), "kllm_chip_plan_prepare")
+        n = C.c_size_t(0)
+        lib().kllm_shard_export(self.ctx, None, 0, C.byref(n))
+        buf = C.create_string_buffer(n.value)
+        check(lib().kllm_shard_export(self.ctx, buf, n.value, C.byref(n)), "kllm_shard_export")
+        return buf.raw[:n.value]
+
+    def final_logits(self) -> np.ndarray:
+        """The logits slot after the last processor_infer step ([vocab])."""
+        n = C.c_int(0)
+        ptr = lib().tape_slot_read(self.ctx, int(self.info["logits_slot"]), C.byref(n))
+        if not ptr:
+            raise KllmError("tape_slot_read: " + last_error())
+        V = int(self.info["vocab_size"])
+        a = np.ctypeslib.as_array(ptr, shape=(n.value,))
+        return a[max(n.value - V, 0):].copy()
+
+    def connect(self, blocks: list) -> None:
+        """Map the other ranks' buffers (blocks from every rank's shard())."""
+        per = len(blocks[0])
+        assert all(len(b) == per for b in blocks)
+        data = b"".join(blocks)
+        check(lib().kllm_shard_connect(self.ctx, data, per), "kllm_shard_connect")
 
     def stats(self) -> dict:
         s = InferStats()

@@ -303,6 +303,17 @@ int kllm_chip_infer(kllm_chip *c, const int *prompt, int prompt_len, int max_new
                            c->layers, c->n_kv, prompt, prompt_len, max_new, eos, out, out_len);
 }
 
+int kllm_chip_plan_prepare(kllm_chip *c) {
+    if (!c) {
+        set_error("kllm_chip_plan_prepare: NULL chip");
+        return -1;
+    }
+    return kllm_plan_prepare(c->ctx, c->embed.data(), c->vocab, c->hidden, c->rope_cos.data(),
+                             c->rope_sin.data(), c->head_dim, c->embed_slot, c->cos_slot,
+                             c->sin_slot, c->kv_in.data(), c->kv_out.data(), c->logits_slot,
+                             c->layers, c->n_kv, c->max_seq);
+}
+
 int kllm_chip_infer_bytes(kllm_chip *c, const uint8_t *in, int len, int max_new, int max_seq,
                           token_callback_fn cb, void *ud, int *total) {
     if (!c) {

@@ -82,6 +82,7 @@ struct CtxImpl {
     kllm_infer_opts opts;
     kllm_infer_stats stats;
     long long launches = 0;      // kernels this context launched
+    int shard_rank = 0, shard_world = 1;   // column shard of the fused decode
 };
 
 static inline CtxImpl *impl(TapeCtx *c) { return reinterpret_cast<CtxImpl *>(c); }

@@ -221,6 +221,64 @@ struct ByteSink : TokenSink {
 };
 }  // namespace
 
+extern "C" int kllm_plan_prepare(TapeCtx *ctx, const float *embed_table, int vocab_size,
+                                 int hidden_dim, const float *rope_cos, const float *rope_sin,
+                                 int head_dim, int token_embed_slot, int rope_cos_slot,
+                                 int rope_sin_slot, const int *kv_in_slots,
+                                 const int *kv_out_slots, int logits_slot, int n_layers,
+                                 int num_kv_heads, int max_pos) {
+    if (!ctx || !embed_table || !rope_cos || !rope_sin || !kv_in_slots || !kv_out_slots ||
+        max_pos < 1) {
+        set_error("kllm_plan_prepare: bad argument");
+        return -1;
+    }
+    CtxImpl *c = impl(ctx);
+    if (!select_device(c)) return -1;
+    PlanDesc pd;
+    pd.embed = embed_table;
+    pd.vocab = vocab_size;
+    pd.hidden = hidden_dim;
+    pd.rope_cos = rope_cos;
+    pd.rope_sin = rope_sin;
+    pd.head_dim = head_dim;
+    pd.embed_slot = token_embed_slot;
+    pd.cos_slot = rope_cos_slot;
+    pd.sin_slot = rope_sin_slot;
+    pd.kv_in = kv_in_slots;
+    pd.kv_out = kv_out_slots;
+    pd.logits_slot = logits_slot;
+    pd.n_layers = n_layers;
+    pd.n_kv = num_kv_heads;
+    std::string why;
+    if (!plan_prepare(c, pd, max_pos, &why)) {
+        if (!why.empty()) set_error("fused decode plan unavailable: %s", why.c_str());
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" int kllm_shard_set(TapeCtx *ctx, int rank, int world) {
+    if (!ctx || world < 1 || rank < 0 || rank >= world) {
+        set_error("kllm_shard_set: rank %d of %d", rank, world);
+        return -1;
+    }
+    CtxImpl *c = impl(ctx);
+    if (c->shard_rank != rank || c->shard_world != world) plan_destroy(c);
+    c->shard_rank = rank;
+    c->shard_world = world;
+    return 0;
+}
+
+extern "C" int kllm_shard_export(TapeCtx *ctx, void *out, size_t cap, size_t *len) {
+    if (!ctx) return -1;
+    return plan_shard_export(impl(ctx), out, cap, len) ? 0 : -1;
+}
+
+extern "C" int kllm_shard_connect(TapeCtx *ctx, const void *all, size_t per_rank) {
+    if (!ctx) return -1;
+    return plan_shard_connect(impl(ctx), all, per_rank) ? 0 : -1;
+}
+
 extern "C" int processor_infer(TapeCtx *ctx, const float *embed_table, int vocab_size,
                                int hidden_dim, const float *rope_cos, const float *rope_sin,
                                int head_dim, int token_embed_slot, int rope_cos_slot,

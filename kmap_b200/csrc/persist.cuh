@@ -42,12 +42,18 @@
 namespace kllm {
 
 enum DSKind : int { DS_GEMV = 0, DS_ATT = 1 };
+// Buffers every rank of a column-sharded decode holds a full copy of; a rank
+// stores its columns' results into all copies (DSArgs::peers).
+enum DSPeer : int {
+    DSP_Q = 0, DSP_KC, DSP_VC, DSP_HA, DSP_HB, DSP_ACT, DSP_LOGITS, DSP_CANDV, DSP_CANDI,
+    DSP_DONE, DSP_KINDS
+};
 enum DSX : int { DX_EMBED = 0, DX_NORM = 1, DX_VEC = 2 };
 enum DSE : int { DE_QKV = 0, DE_RESID = 1, DE_SWIGLU = 2, DE_LM = 3 };
 
 struct DSPhase {
     int kind, ntasks;          // GEMV: column groups; attention: heads
-    int dep, dep_count;        // wait for done[dep] >= dep_count (dep < 0: none)
+    int dep, dep_count;        // wait for done[dep] >= dep_count per step (dep < 0: none)
     TTXDesc d;                 // GEMV layout (ttx.cuh)
     int npieces;               // 16-step pieces per group
     int xs;                    // floats per chunk row of the staged x
@@ -60,14 +66,18 @@ struct DSPhase {
     const float *norm_w;
     float eps;
     const float *hold;         // DE_RESID: residual in (nullptr: embedding row)
-    float *out;                // q / new residual / act / logits
+    float *out;                // q / new residual / act / logits (this rank's copy)
+    int out_kind;              // DSPeer of out
+    int groups_all;            // column groups of the matrix over all ranks
     int layer;
 };
 
 struct DSArgs {
     const DSPhase *phases;
     int nphases;
-    int *done;                 // [nphases] arrivals (zeroed per step)
+    int *done;                 // [nphases] arrivals, counting up across steps
+    int *epoch;                // steps completed since the counters were zeroed
+    int *lm_local;             // lm_head arrivals of this rank's CTAs only
     int *status;
     int *abort;
     int stages, tab_cap, wn_cap, xc_cap;
@@ -88,9 +98,29 @@ struct DSArgs {
     // lm_head
     float *hist;
     int hist_rows;
-    float *cand_v;             // [G] per-CTA first maxima
+    float *cand_v;             // [world][G] per-CTA first maxima
     int *cand_i;
+    // column sharding: this rank, the ranks, and [DSP_KINDS][world] pointers
+    // to every rank's copy of the shared buffers (this rank's own included)
+    int rank, world;
+    void *const *peers;
 };
+
+template <class T>
+__device__ __forceinline__ T *ds_peer(const DSArgs &a, int kind, int r) {
+    return reinterpret_cast<T *>(a.peers[kind * a.world + r]);
+}
+
+// Store v at index i of every rank's copy of buffer `kind`.
+__device__ __forceinline__ void ds_put(const DSArgs &a, int kind, size_t i, float v) {
+    for (int r = 0; r < a.world; r++) ds_peer<float>(a, kind, r)[i] = v;
+}
+
+// CTAs of rank r with work in a phase of `groups_all` column groups.
+__device__ __forceinline__ int ds_ncta(const DSArgs &a, int groups_all, int r, int G) {
+    const int local = r < groups_all ? (groups_all - r + a.world - 1) / a.world : 0;
+    return min(G, local);
+}
 
 constexpr int DS_NCW = 8;                    // consumer warps
 constexpr int DS_NC = DS_NCW * 32;
@@ -104,7 +134,7 @@ constexpr int DS_STAGE = DS_PIECE_STEPS * TTX_STEP;
 
 __device__ __forceinline__ int ld_acquire(const int *p) {
     int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -390,6 +420,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     // =============================================================== consumers
     const int tid = threadIdx.x;
     const int t = lane & 7, cp = lane >> 3;    // chunk, column pair
+    // The arrival counters are never reset between steps: this step's
+    // targets are (epoch + 1) times a phase's per-step count.
+    const int ep1 = *a.epoch + 1;
     int seq_base = 0, q = 0;
     float lm_v = -INFINITY;                    // this warp's first maximum
     int lm_i = -1;
@@ -399,7 +432,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         bool bad = false;
         if (tid == 0) {
             bool ok = !ld_acquire(a.abort);
-            if (ok && ph.dep >= 0) ok = ds_wait_counter(a.done + ph.dep, ph.dep_count, a.status, a.abort);
+            if (ok && ph.dep >= 0)
+                ok = ds_wait_counter(a.done + ph.dep, ph.dep_count * ep1, a.status, a.abort);
             s_flag = ok ? 1 : 0;
         }
         cbar_sync();
@@ -474,7 +508,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             for (int j = warp; j < J; j += DS_NCW) {
                 const int r = j / DS_NCW, nr = min(DS_NCW, J - DS_NCW * r);
                 const int m = j / W, w = j % W;
-                const int g = cta + m * G;
+                const int g = (cta + m * G) * a.world + a.rank;   // the matrix's group
                 const int ch = DS_NCW * w + t;        // this lane's chunk
                 const int len = d.chunk_len(ch);
                 const float *xr = ch < d.T ? xc + ch * xs : xc;
@@ -561,19 +595,19 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                                 const float rt = cp < 2 ? -pp[k] : pp[k];
                                 const float v = __fadd_rn(__fmul_rn(yy[k], cc[k]), __fmul_rn(rt, sn2[k]));
                                 if (head < a.nh)
-                                    a.q[n] = v;
+                                    ds_put(a, DSP_Q, n, v);
                                 else
-                                    a.kc[(((size_t)ph.layer * a.nkv + (head - a.nh)) * a.max_pos + pos) * HD + dim] = v;
+                                    ds_put(a, DSP_KC, (((size_t)ph.layer * a.nkv + (head - a.nh)) * a.max_pos + pos) * HD + dim, v);
                             } else {
                                 const int vi = n - a.qd - a.kvd;
-                                a.vc[(((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD] = yy[k];
+                                ds_put(a, DSP_VC, (((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD, yy[k]);
                             }
                         }
                     }
                 } else if (ph.emode == DE_RESID) {
                     if (t == 0 && !bad) {
-                        if (n0 >= 0) ph.out[n0] = __fadd_rn(ea.x, y.x);
-                        if (n1 >= 0) ph.out[n1] = __fadd_rn(ea.y, y.y);
+                        if (n0 >= 0) ds_put(a, ph.out_kind, n0, __fadd_rn(ea.x, y.x));
+                        if (n1 >= 0) ds_put(a, ph.out_kind, n1, __fadd_rn(ea.y, y.y));
                     }
                 } else if (ph.emode == DE_SWIGLU) {
                     float2 up;
@@ -586,7 +620,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         for (int k = 0; k < 2; k++) {
                             if (nn[k] < 0) continue;
                             const double dg = (double)yy[k];
-                            ph.out[nn[k]] = __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]);
+                            ds_put(a, ph.out_kind, nn[k], __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]));
                         }
                     }
                 } else {   // DE_LM
@@ -597,7 +631,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         for (int k = 0; k < 2; k++) {
                             const int n = nn[k];
                             if (n < 0) continue;
-                            ph.out[n] = yy[k];
+                            ds_put(a, ph.out_kind, n, yy[k]);
                             if (a.hist && pos < a.hist_rows) a.hist[(size_t)pos * d.N + n] = yy[k];
                             if (yy[k] > lm_v || (yy[k] == lm_v && lm_i >= 0 && n < lm_i)) {
                                 lm_v = yy[k];
@@ -636,30 +670,56 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                             bi = oi;
                         }
                     }
-                    a.cand_v[cta] = bv;
-                    a.cand_i[cta] = bi;
+                    for (int r = 0; r < a.world; r++) {
+                        ds_peer<float>(a, DSP_CANDV, r)[a.rank * G + cta] = bv;
+                        ds_peer<int>(a, DSP_CANDI, r)[a.rank * G + cta] = bi;
+                    }
                 }
             }
             if (tid == 0) {
-                __threadfence();
-                const int prev = atomicAdd(a.done + p, 1);
-                const int ncta = min(G, ph.ntasks);
-                if (ph.emode == DE_LM && prev == ncta - 1) {
+                // arrive at every rank's counter of this phase
+                int ncta = 0;
+                for (int r = 0; r < a.world; r++) ncta += ds_ncta(a, ph.groups_all, r, G);
+                int prev = 0;
+                if (a.world == 1) {
+                    __threadfence();
+                    prev = atomicAdd(a.done + p, 1);
+                } else {
+                    __threadfence_system();
+                    for (int r = 0; r < a.world; r++) {
+                        const int o = atomicAdd_system(ds_peer<int>(a, DSP_DONE, r) + p, 1);
+                        if (r == a.rank) prev = o;
+                    }
+                }
+                // the token pick runs on every rank: by the last CTA of
+                // this rank to arrive, once every rank's candidates are in
+                bool pick = false;
+                if (ph.emode == DE_LM) {
+                    if (a.world == 1) {
+                        pick = prev == ncta * ep1 - 1;
+                    } else {
+                        const int pl = atomicAdd(a.lm_local, 1);
+                        pick = pl == ds_ncta(a, ph.groups_all, a.rank, G) * ep1 - 1 &&
+                               ds_wait_counter(a.done + p, ncta * ep1, a.status, a.abort);
+                    }
+                }
+                if (pick) {
                     // the reference's greedy pick: best = logits[0], then
                     // strict > over the rest in index order
-                    __threadfence();
+                    __threadfence_system();
                     const float l0 = __ldcg(ph.out);
                     int bidx = 0;
                     if (!(l0 != l0)) {
                         float best = l0;
-                        for (int c = 0; c < ncta; c++) {
-                            const float cv = __ldcg(a.cand_v + c);
-                            const int ci = __ldcg(a.cand_i + c);
-                            if (ci >= 0 && (cv > best || (cv == best && ci < bidx))) {
-                                best = cv;
-                                bidx = ci;
+                        for (int r = 0; r < a.world; r++)
+                            for (int c = 0; c < ds_ncta(a, ph.groups_all, r, G); c++) {
+                                const float cv = __ldcg(a.cand_v + r * G + c);
+                                const int ci = __ldcg(a.cand_i + r * G + c);
+                                if (ci >= 0 && (cv > best || (cv == best && ci < bidx))) {
+                                    best = cv;
+                                    bidx = ci;
+                                }
                             }
-                        }
                     }
                     const int P0 = a.st->prompt_len;
                     if (pos >= P0 - 1) {
@@ -672,6 +732,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         a.st->n_gen = gi + 1;
                     }
                     a.st->pos = pos + 1;
+                    *a.epoch = ep1;
                 }
             }
         } else {   // ============================================ attention

@@ -492,10 +492,16 @@ struct DecodePlan {
     DSArgs ds = {};
     std::vector<DSPhase> phases;
     DSPhase *d_phases = nullptr;
-    int *d_cnt = nullptr;          // done[phases] + tile counters, zeroed per step
+    int *d_cnt = nullptr;          // done[phases] then the epoch (zero only when built)
     size_t cnt_n = 0;
     int *d_abort = nullptr;
     std::vector<void *> ds_bufs;   // device layouts, partials, activations
+    // column shard: every rank's copy of the shared buffers ([kind][rank])
+    int rank = 0, world = 1;
+    bool connected = false;
+    std::vector<void *> peer_host;   // host copy of the table
+    void **d_peers = nullptr;
+    std::vector<void *> opened;      // peers' buffers mapped into this process
     long long kernels_per_step = 0;
     int graph_hist_rows = 0;
     int logits_slot = -1;
@@ -516,7 +522,9 @@ static void free_plan(DecodePlan *p) {
         if (b) cudaFree(b);
     for (void *b : p->ds_bufs)
         if (b) cudaFree(b);
-    for (void *b : {(void *)p->d_phases, (void *)p->d_cnt, (void *)p->d_abort})
+    for (void *b : p->opened)
+        if (b) cudaIpcCloseMemHandle(b);
+    for (void *b : {(void *)p->d_phases, (void *)p->d_cnt, (void *)p->d_abort, (void *)p->d_peers})
         if (b) cudaFree(b);
     if (p->gen_host) cudaFreeHost(p->gen_host);
     for (cudaEvent_t e : {p->ev0, p->ev1, p->ev2})
@@ -571,7 +579,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     std::vector<TTXDesc> desc(nmat);
     std::vector<uint8_t *> streams(nmat);
     std::vector<float *> tables(nmat);
-    std::vector<int> xsz(nmat);
+    std::vector<int> xsz(nmat), groups_all(nmat);
+    const int rank = c->shard_rank, world = c->shard_world;
     int tab_cap = 0, xc_cap = (p->max_pos + 3) & ~3;
     auto own = [&](void *b) { p->ds_bufs.push_back(b); };
     for (int i = 0; i < nmat; i++) {
@@ -583,7 +592,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         // one round of warp tasks (decode tolerance instead of bit-exact sums)
         int W = 1;
         if (p->order == KLLM_ORDER_FAST) {
-            const int ng = mode == TTX_GATE_UP ? (sl.tt_N / 2 + 3) / 4 : (sl.tt_N + 7) / 8;
+            const int ng =
+                ((mode == TTX_GATE_UP ? (sl.tt_N / 2 + 3) / 4 : (sl.tt_N + 7) / 8) + world - 1) / world;
             while (W < 8 && (long long)ng * 2 * W <= (long long)sms * DS_NCW &&
                    sl.tt_K % (16 * 8 * W) == 0)
                 W *= 2;
@@ -591,6 +601,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, hd, t.nh + nkv, max_table, max_r, W,
                           &desc[i]))
             return false;
+        groups_all[i] = desc[i].ngroups;
+        if (c->shard_world > 1) ttx_shard(&desc[i], c->shard_rank, c->shard_world);
         const TTXDesc &d = desc[i];
         if (!KLLM_CUDA(cudaMalloc((void **)&streams[i], d.stream_bytes()))) return false;
         own(streams[i]);
@@ -631,12 +643,20 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     };
     float *qb = fbuf(qd), *act = fbuf(t.F), *hA = fbuf(H), *hB = fbuf(H);
     if (!qb || !act || !hA || !hB) return false;
-    if (sms > 1024) return false;   // lm_head candidates, one per CTA
+    if ((size_t)sms * world > 4096) return false;   // lm_head candidates, one per CTA and rank
     // phases
     std::vector<DSPhase> ph;
-    auto ncta = [&](int ntasks) { return std::min(sms, ntasks); };
+    // CTAs of all ranks with work in a matrix's phase (each arrives once)
+    auto ncta = [&](int mi) {
+        int n = 0;
+        for (int r = 0; r < world; r++) {
+            const int local = r < groups_all[mi] ? (groups_all[mi] - r + world - 1) / world : 0;
+            n += std::min(sms, local);
+        }
+        return n;
+    };
     auto gemv = [&](int mi, int xmode, const float *x, const float *nw, float eps, int emode,
-                    const float *hold, float *out, int dep, int dep_count, int layer) {
+                    const float *hold, float *out, int out_kind, int dep, int dep_count, int layer) {
         const TTXDesc &d = desc[mi];
         DSPhase m = {};
         m.kind = DS_GEMV;
@@ -657,6 +677,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         m.eps = eps;
         m.hold = hold;
         m.out = out;
+        m.out_kind = out_kind;
+        m.groups_all = groups_all[mi];
         m.layer = layer;
         ph.push_back(m);
         return (int)ph.size() - 1;
@@ -666,28 +688,28 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         const int mq = 4 * l;
         const int p_qkv =
             l == 0 ? gemv(mq, DX_EMBED, nullptr, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr,
-                          qb, -1, 0, l)
+                          qb, DSP_Q, -1, 0, l)
                    : gemv(mq, DX_NORM, hA, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr, qb,
-                          prev_dn, ncta(desc[mq - 1].ngroups), l);
+                          DSP_Q, prev_dn, ncta(mq - 1), l);
         DSPhase at = {};
         at.kind = DS_ATT;
         at.ntasks = t.nh;
         at.dep = p_qkv;
-        at.dep_count = ncta(desc[mq].ngroups);
+        at.dep_count = ncta(mq);
         at.layer = l;
         ph.push_back(at);
         const int p_att = (int)ph.size() - 1;
         const int p_o = gemv(mq + 1, DX_VEC, p->ctx, nullptr, 0.f, DE_RESID, l == 0 ? nullptr : hA,
-                             hB, p_att, t.nh, l);
+                             hB, DSP_HB, p_att, t.nh, l);
         const int p_gu = gemv(mq + 2, DX_NORM, hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1],
-                              DE_SWIGLU, nullptr, act, p_o, ncta(desc[mq + 1].ngroups), l);
-        prev_dn = gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, hB, hA, p_gu,
-                       ncta(desc[mq + 2].ngroups), l);
+                              DE_SWIGLU, nullptr, act, DSP_ACT, p_o, ncta(mq + 1), l);
+        prev_dn = gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, hB, hA, DSP_HA, p_gu,
+                       ncta(mq + 2), l);
     }
-    gemv(nmat - 1, DX_NORM, hA, p->dev_norm.back(), p->f_eps, DE_LM, nullptr, p->logits, prev_dn,
-         ncta(desc[nmat - 2].ngroups), L);
+    gemv(nmat - 1, DX_NORM, hA, p->dev_norm.back(), p->f_eps, DE_LM, nullptr, p->logits, DSP_LOGITS,
+         prev_dn, ncta(nmat - 2), L);
     const size_t nph = ph.size();
-    p->cnt_n = nph;
+    p->cnt_n = nph + 2;   // done[phases], epoch, this rank's lm_head arrivals
     if (!KLLM_CUDA(cudaMalloc((void **)&p->d_cnt, p->cnt_n * sizeof(int))) ||
         !KLLM_CUDA(cudaMemset(p->d_cnt, 0, p->cnt_n * sizeof(int))) ||
         !KLLM_CUDA(cudaMalloc((void **)&p->d_phases, nph * sizeof(DSPhase))) ||
@@ -697,10 +719,26 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         !KLLM_CUDA(cudaMemset(p->d_abort, 0, sizeof(int))))
         return false;
     p->phases = ph;
+    // this rank's shared buffers; the other ranks' arrive with shard_connect
+    p->rank = rank;
+    p->world = world;
+    p->peer_host.assign((size_t)DSP_KINDS * world, nullptr);
+    {
+        void *mine[DSP_KINDS] = {qb, p->kc, p->vc, hA, hB, act, p->logits, p->cand_v, p->cand_i,
+                                 p->d_cnt};
+        for (int k = 0; k < DSP_KINDS; k++) p->peer_host[(size_t)k * world + rank] = mine[k];
+    }
+    if (!KLLM_CUDA(cudaMalloc((void **)&p->d_peers, p->peer_host.size() * sizeof(void *))) ||
+        !KLLM_CUDA(cudaMemcpy(p->d_peers, p->peer_host.data(), p->peer_host.size() * sizeof(void *),
+                              cudaMemcpyHostToDevice)))
+        return false;
+    p->connected = world == 1;
     DSArgs &a = p->ds;
     a.phases = p->d_phases;
     a.nphases = (int)nph;
     a.done = p->d_cnt;
+    a.epoch = p->d_cnt + nph;
+    a.lm_local = p->d_cnt + nph + 1;
     a.status = p->status;
     a.abort = p->d_abort;
     a.stages = S;
@@ -730,10 +768,70 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.ctx = p->ctx;
     a.cand_v = p->cand_v;
     a.cand_i = p->cand_i;
+    a.rank = rank;
+    a.world = world;
+    a.peers = p->d_peers;
     p->ds_grid = sms;
     p->ds_stages = S;
     p->ds_smem = smem;
     p->persist = true;
+    return true;
+}
+
+// Column shard: IPC handles of this rank's shared buffers, in DSPeer order.
+bool plan_shard_export(CtxImpl *c, void *out, size_t cap, size_t *len) {
+    DecodePlan *p = c->plan;
+    const size_t need = (size_t)DSP_KINDS * sizeof(cudaIpcMemHandle_t);
+    if (len) *len = need;
+    if (!p || !p->persist) {
+        set_error("kllm_shard_export: no fused decode plan (prepare it first)");
+        return false;
+    }
+    if (!out && cap == 0) return true;   // size query
+    if (!out || cap < need) {
+        set_error("kllm_shard_export: buffer of %zu bytes, %zu needed", cap, need);
+        return false;
+    }
+    cudaSetDevice(c->device);
+    for (int k = 0; k < DSP_KINDS; k++) {
+        cudaIpcMemHandle_t h;
+        if (!KLLM_CUDA(cudaIpcGetMemHandle(&h, p->peer_host[(size_t)k * p->world + p->rank])))
+            return false;
+        memcpy(static_cast<char *>(out) + k * sizeof h, &h, sizeof h);
+    }
+    return true;
+}
+
+// Map every other rank's shared buffers (world blocks of the export format,
+// rank order) and publish the full table to the kernel.
+bool plan_shard_connect(CtxImpl *c, const void *all, size_t per_rank) {
+    DecodePlan *p = c->plan;
+    if (!p || !p->persist) {
+        set_error("kllm_shard_connect: no fused decode plan (prepare it first)");
+        return false;
+    }
+    if (!all || per_rank < (size_t)DSP_KINDS * sizeof(cudaIpcMemHandle_t)) {
+        set_error("kllm_shard_connect: malformed handle block");
+        return false;
+    }
+    if (p->connected) return true;
+    cudaSetDevice(c->device);
+    for (int r = 0; r < p->world; r++) {
+        if (r == p->rank) continue;
+        for (int k = 0; k < DSP_KINDS; k++) {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, static_cast<const char *>(all) + r * per_rank + k * sizeof h, sizeof h);
+            void *ptr = nullptr;
+            if (!KLLM_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess)))
+                return false;
+            p->opened.push_back(ptr);
+            p->peer_host[(size_t)k * p->world + r] = ptr;
+        }
+    }
+    if (!KLLM_CUDA(cudaMemcpy(p->d_peers, p->peer_host.data(), p->peer_host.size() * sizeof(void *),
+                              cudaMemcpyHostToDevice)))
+        return false;
+    p->connected = true;
     return true;
 }
 
@@ -747,7 +845,8 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     DecodePlan *old = c->plan;
     if (old && old->max_pos >= max_pos && old->src_embed == d.embed &&
         old->src_cos == d.rope_cos && old->src_sin == d.rope_sin && old->ti.H == d.hidden &&
-        old->ti.V == d.vocab && old->order == c->opts.order) {
+        old->ti.V == d.vocab && old->order == c->opts.order && old->rank == c->shard_rank &&
+        old->world == c->shard_world) {
         return true;   // reuse (weights are re-checked by upload_tt below)
     }
     TemplateInfo ti;
@@ -868,7 +967,7 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
     if (!dalloc(&p->h, H) || !dalloc(&p->qkv, nq) || !dalloc(&p->ctx, qd) ||
         !dalloc(&p->act, F) || !dalloc(&p->logits, V) || !dalloc(&p->part, part_n) ||
         !dalloc(&p->counters, n_cnt) || !dalloc(&p->kc, kv) || !dalloc(&p->vc, kv) ||
-        !dalloc(&p->cand_v, 1024) || !dalloc(&p->cand_i, 1024) || !dalloc(&p->st, 1) ||
+        !dalloc(&p->cand_v, 4096) || !dalloc(&p->cand_i, 4096) || !dalloc(&p->st, 1) ||
         !dalloc(&p->prompt, max_pos) || !dalloc(&p->gen, max_pos) || !dalloc(&p->status, 1))
         return fail();
     if (!KLLM_CUDA(cudaMemset(p->kc, 0, kv * 4)) || !KLLM_CUDA(cudaMemset(p->vc, 0, kv * 4)) ||
@@ -921,10 +1020,14 @@ static bool launch_pdl(cudaStream_t s, Kern kern, dim3 grid, dim3 block, size_t 
 // One tape step as a single cooperative launch (arrival counters cleared
 // first).
 static bool record_step_persist(CtxImpl *c, DecodePlan *p) {
+    if (!p->connected) {
+        set_error("column-sharded decode: the ranks' buffers are not connected "
+                  "(kllm_shard_export / kllm_shard_connect)");
+        return false;
+    }
     DSArgs a = p->ds;
     a.hist = p->hist;
     a.hist_rows = p->hist_rows;
-    if (!KLLM_CUDA(cudaMemsetAsync(p->d_cnt, 0, p->cnt_n * sizeof(int), c->stream))) return false;
     auto kern = p->ti.hd == 32 ? k_decode_step<32>
                                : p->ti.hd == 64 ? k_decode_step<64> : k_decode_step<128>;
     cudaLaunchConfig_t cfg = {};
@@ -1132,6 +1235,8 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
     int status = 0;
     if (!KLLM_CUDA(cudaMemcpy(&status, p->status, 4, cudaMemcpyDeviceToHost))) return false;
     if (status) {
+        // an aborted step leaves the arrival counters mid-step: start over
+        if (p->d_cnt) cudaMemset(p->d_cnt, 0, p->cnt_n * sizeof(int));
         set_error("decode kernels reported status 0x%x (%s)", status,
                   (status & ST_WAIT_TIMEOUT) ? "a wait timed out" : "a token was out of range");
         return false;

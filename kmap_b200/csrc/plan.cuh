@@ -26,6 +26,9 @@ bool plan_match(const TapeCtx *ctx, const PlanDesc &d, std::string *why);
 // (weights, KV cache for max_pos positions, graphs).  Returns false with a
 // reason when the tape is not the template; no error is recorded then.
 bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why);
+// Column-sharded decode: export this rank's shared buffers, map the others'.
+bool plan_shard_export(CtxImpl *c, void *out, size_t cap, size_t *len);
+bool plan_shard_connect(CtxImpl *c, const void *all, size_t per_rank);
 
 // Prefill + greedy decode on the plan.  emit(token, i) is called for every
 // generated token in order and returns false to stop.

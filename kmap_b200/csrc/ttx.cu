@@ -33,6 +33,8 @@ bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads
     } else {
         t.ngroups = (N + TTX_GCOLS - 1) / TTX_GCOLS;
     }
+    t.gstride = 1;
+    t.goff = 0;
     t.npad = (n_codes + 31) & ~31;
     // slots are byte offsets into the table: R * npad * 4 must fit 16 bits
     int r = 4;
@@ -43,6 +45,12 @@ bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads
     t.R = r;
     *d = t;
     return true;
+}
+
+void ttx_shard(TTXDesc *d, int rank, int world) {
+    d->ngroups = rank < d->ngroups ? (d->ngroups - rank + world - 1) / world : 0;
+    d->gstride = world;
+    d->goff = rank;
 }
 
 // One thread per warp-wide gather of the decode kernel: group g, sub-task w,
@@ -58,8 +66,8 @@ __global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
     const int e = (int)(gid & 7), k = (int)((gid >> 3) & 1);
     const long long gs = gid >> 4;
     const int s = (int)(gs % d.ns);
-    const long long gw = gs / d.ns;          // g * W + w
-    const int g = (int)(gw / d.W), w = (int)(gw % d.W);
+    const long long gw = gs / d.ns;          // i * W + w, i a stored group
+    const int g = (int)(gw / d.W) * d.gstride + d.goff, w = (int)(gw % d.W);
 
     int code[32];   // distinct codes
     int lane_u[32];
@@ -158,7 +166,8 @@ __global__ void k_ttx_table(const float *__restrict__ cb, const TTXDesc d, float
 bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDesc &d,
                uint8_t *stream, float *table) {
     const long long ngather = (long long)d.ngroups * d.W * d.ns * 16;
-    if (ngather <= 0) return false;
+    if (ngather < 0) return false;
+    if (ngather == 0) return true;   // a rank without groups of this matrix
     const int bs = 128;
     k_ttx_build<<<(unsigned)((ngather + bs - 1) / bs), bs, 0, s>>>(idx, d, stream, ngather);
     if (!KLLM_CUDA(cudaGetLastError())) return false;

@@ -27,6 +27,8 @@
 //    (its own NS steps, lane chunk 8w + lane % 8) goes to its own warp, and
 //    the W partial sums are added in w order.  Same bytes, W times the
 //    warps; the sums are no longer the reference's bit for bit.
+//  * Column shards.  A rank of a multi-GPU decode stores only its groups:
+//    group i of its stream is group i * world + rank of the matrix.
 //  * Column groups.  Plain matrices take 8 consecutive columns.  gate_up
 //    (N = 2F) takes gate columns 4g..4g+3 and the matching up columns, so a
 //    group holds both inputs of its SwiGLU.  QKV with RoPE takes, inside one
@@ -48,7 +50,8 @@ struct TTXDesc {
     int T, base, rem;     // the chunking of K (the reference's when W == 1)
     int W;                // sub-tasks (warps) per group
     int ns;               // steps per group (8 rows of every chunk per step)
-    int ngroups;
+    int ngroups;          // groups stored here (a column shard: every gstride-th)
+    int gstride, goff;    // stored group i is group i * gstride + goff of the matrix
     int R, npad;          // codebook copies, entries per copy (multiple of 32)
     int colmode;
     int F;                // TTX_GATE_UP: N == 2F
@@ -98,6 +101,8 @@ __host__ __device__ inline int ttx_col(const TTXDesc &d, int g, int c) {
 // splits each group into that many sub-tasks (fast order).
 bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads,
                   int max_table_bytes, int max_r, int split_w, TTXDesc *d);
+// Restrict d to the column groups of one rank (group g with g % world == rank).
+void ttx_shard(TTXDesc *d, int rank, int world);
 // Build the slot stream and (table != nullptr) the replicated table on the
 // device.
 bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDesc &d,
