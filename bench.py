@@ -281,7 +281,11 @@ def run_ours(args, rank, world, local_rank):
     chip_path = config0_chip(rank)
     order = kmap_b200.ORDER_FAST if args.order == "fast" else kmap_b200.ORDER_EXACT
     chip = kmap_b200.Chip(chip_path, order=order)
-    p = prompt_ids(seed=rank)
+    shard = args.shard and world > 1
+    if shard:   # every rank holds 1/world of the columns; same prompt everywhere
+        chip.connect(kmap_b200.exchange_blocks(chip.shard(rank, world)))
+        dist.barrier()
+    p = prompt_ids(seed=0 if shard else rank)
     t0 = time.time()
     chip.infer(p, GEN)      # first call prepares the plan (weights to HBM, graph)
     st = chip.stats()
@@ -315,8 +319,9 @@ def run_ours(args, rank, world, local_rank):
         if dist:
             dist.destroy_process_group()
         return
-    value = tokens * world / (dev_ms_max / 1e3)
-    e2e = tokens * world / (host_ms_max / 1e3)
+    streams = 1 if shard else world   # sharded: one stream over all GPUs
+    value = tokens * streams / (dev_ms_max / 1e3)
+    e2e = tokens * streams / (host_ms_max / 1e3)
     pk = peaks()
     hbm = pk.get("hbm_gbs")
     roof = ttgemv_roofline(local_rank)
@@ -325,6 +330,8 @@ def run_ours(args, rank, world, local_rank):
     # its algorithmic bytes are the index stream of every TT matrix
     step_us = dev_ms_max * 1e3 / tokens
     decode_gbs = INDEX_BYTES_PER_TOKEN / (step_us * 1e-6) / 1e9
+    # sharded: the index stream is split over the GPUs, so their summed peak
+    roof_peak = hbm * world if (shard and hbm) else hbm
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = reference_sample(chip_path)
@@ -332,18 +339,20 @@ def run_ours(args, rank, world, local_rank):
         "metric": "decode tok/s (prompt + generated tape steps per second)",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if shard else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
         "config": {"workload": "TinyLlama-1.1B-arch TT chip (22x2048, 32/4 heads, SwiGLU 5632, "
                    "vocab 32000, bf16-rounded N(0,0.02)), batch-1 greedy decode",
                    "prompt": PROMPT, "generate": GEN, "tape_steps_per_call": PROMPT + GEN,
                    "l2": "weights 2.07 GB/token >> 126 MB L2 (no flush needed)",
-                   "parallelism": "replicas" if world > 1 else "single GPU"},
+                   "parallelism": ("column-sharded over %d GPUs (NVLink peer stores in the "
+                                   "decode kernel)" % world if shard else
+                                   "replicas" if world > 1 else "single GPU")},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                 "d2h_bytes_per_step": GEN * 4},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "achieved": decode_gbs, "peak": hbm, "unit": "GB/s",
-                     "frac": decode_gbs / hbm if hbm else None,
+        "roofline": {"bound": "hbm", "achieved": decode_gbs, "peak": roof_peak, "unit": "GB/s",
+                     "frac": decode_gbs / roof_peak if roof_peak else None,
                      "traffic": STEP_TRAFFIC_BYTES,
                      "kernel": "k_decode_step", "launch_us": step_us,
                      "algorithmic_bytes_per_launch": INDEX_BYTES_PER_TOKEN,
@@ -373,6 +382,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", action="store_true",
+                    help="with N > 1: one decode stream column-sharded over the N GPUs "
+                         "(strong scaling) instead of N independent replicas")
     ap.add_argument("--order", default="exact", choices=["exact", "fast"],
                     help="TT-GEMV summation order of the decode step: the reference's "
                          "chunked order (bit-identical MATMUL_TT) or the finer split")
