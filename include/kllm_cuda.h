@@ -82,7 +82,12 @@ typedef struct {
     double decode_ms;        /* device time of the generation steps */
     double total_ms;         /* wall time inside the call */
     long long launches;      /* kernels launched inside the call */
-    int reserved[8];
+    int step_kernel;         /* fused: 1 = one persistent kernel per tape step,
+                                0 = the per-kernel plan */
+    int stream_values;       /* persistent step: what the weight streams hold,
+                                0 = codebook table slots, 1 = bf16 values,
+                                2 = fp16 values (exact codebooks only) */
+    int reserved[6];
 } kllm_infer_stats;
 
 void kllm_default_infer_opts(kllm_infer_opts *o);

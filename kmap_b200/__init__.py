@@ -146,7 +146,8 @@ class InferOpts(C.Structure):
 class InferStats(C.Structure):
     _fields_ = [("fused", C.c_int), ("steps", C.c_int), ("prefill_ms", C.c_double),
                 ("decode_ms", C.c_double), ("total_ms", C.c_double),
-                ("launches", C.c_longlong), ("reserved", C.c_int * 8)]
+                ("launches", C.c_longlong), ("step_kernel", C.c_int),
+                ("stream_values", C.c_int), ("reserved", C.c_int * 6)]
 
 
 MODE_AUTO, MODE_GENERIC, MODE_FUSED = 0, 1, 2

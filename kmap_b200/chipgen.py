@@ -92,6 +92,11 @@ class ModelSpec:
     #: "ones" (HF init) or "random" (1 + N(0, 0.1), bf16-rounded): the
     #: random form makes norm-weight handling visible in parity tests.
     norm_weights: str = "ones"
+    #: number format of the matrix weights: "bf16" (the checkpoints the
+    #: benchmarks stand for), "fp16", or "pool4096" (every matrix draws from
+    #: its own 4096 fp32 values, as a quantised codebook would: neither bf16
+    #: nor fp16 numbers).
+    weight_values: str = "bf16"
     model_name: str = "random-init"
 
     @property
@@ -139,9 +144,21 @@ class WeightSource:
         return np.random.default_rng([self.spec.seed, key, len(name)])
 
     def matrix(self, name: str, rows: int, cols: int) -> np.ndarray:
-        """HF-layout ``(out, in)`` weight, bf16-rounded N(0, std)."""
-        g = self._rng(name).standard_normal((rows, cols), dtype=np.float32)
-        g *= np.float32(self.spec.weight_std)
+        """HF-layout ``(out, in)`` weight: N(0, std) in the spec's number format."""
+        rng = self._rng(name)
+        std = np.float32(self.spec.weight_std)
+        kind = self.spec.weight_values
+        if kind == "pool4096":
+            pool = np.sort(rng.standard_normal(4096, dtype=np.float32) * std)
+            return pool[rng.integers(0, 4096, (rows, cols))]
+        g = rng.standard_normal((rows, cols), dtype=np.float32)
+        g *= std
+        if kind == "fp16":
+            out = g.astype(np.float16).astype(np.float32)
+            out[out == 0] = 0.0
+            return out
+        if kind != "bf16":
+            raise ValueError("weight_values must be bf16, fp16 or pool4096")
         return bf16_round(g)
 
     def norm(self, name: str, n: int) -> np.ndarray:
@@ -690,6 +707,8 @@ def ensure_chip(cache_root: str, spec: ModelSpec, log=None) -> str:
         spec.num_layers, spec.hidden_size, spec.num_attention_heads,
         spec.num_key_value_heads, spec.intermediate_size, spec.vocab_size,
         spec.max_seq, spec.seed, spec.norm_weights)
+    if spec.weight_values != "bf16":
+        key += "_" + spec.weight_values
     path = os.path.join(cache_root, key)
     done = os.path.join(path, ".complete")
     if not os.path.exists(done):

@@ -170,6 +170,9 @@ static bool infer_dispatch(CtxImpl *c, const InferArgs &a, const int *prompt, in
         pd.n_kv = a.n_kv;
         std::string why;
         fused = plan_prepare(c, pd, max_pos, &why);
+        if (!fused && mode == KLLM_MODE_AUTO && !why.empty() && getenv("KLLM_VERBOSE") &&
+            atoi(getenv("KLLM_VERBOSE")))
+            fprintf(stderr, "kllm: fused decode plan unavailable: %s\n", why.c_str());
         if (!fused && mode == KLLM_MODE_FUSED) {
             set_error("fused decode plan unavailable: %s", why.c_str());
             return false;
@@ -182,6 +185,9 @@ static bool infer_dispatch(CtxImpl *c, const InferArgs &a, const int *prompt, in
         ok = infer_generic(c, a, prompt, prompt_len, max_new, max_pos, sink, generated);
     }
     c->stats.fused = fused ? 1 : 0;
+    c->stats.step_kernel = 0;
+    c->stats.stream_values = 0;
+    if (fused) plan_kind(c, &c->stats.step_kernel, &c->stats.stream_values);
     c->stats.launches = g_launches - l0;
     c->stats.total_ms =
         std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();

@@ -1,29 +1,32 @@
 // persist.cuh -- the persistent decode step: one cooperative launch runs a
 // whole tape step of the compiler's LLaMA template.
 //
-// Grid = one CTA per SM (co-resident: cooperative launch).  Each CTA has one
-// producer warp and four consumer warps.  The step is a list of phases; per
-// layer QKV, attention, O, gate_up, down; then lm_head.  A GEMV task is one
-// column group (8 columns x all chunks, ttx.cuh) for one warp; task i of a
-// phase goes to CTA i mod G, and a CTA deals its tasks to its warps in turn.
+// Grid = one CTA per SM (co-resident: cooperative launch).  Each CTA has
+// eight consumer warps, a producer warp and a table warp.  The step is a
+// list of phases; per layer QKV, attention, O, gate_up, down; then lm_head.
+// A GEMV task is one column group (8 columns x all chunks, ttx.cuh) for one
+// warp, or one of its W sub-tasks in the fast order; group i of a phase
+// goes to CTA i mod G, and a CTA deals its tasks to its warps in turn.
 //
-// Producer warp: lane 0 streams the CTA's tasks' slot streams through a ring
-// of 16 KB stages with bulk copies, in the order the warps consume them
-// (rounds of up to four tasks, piece by piece).  Weights do not depend on
-// activations, so the stream runs ahead across phase boundaries.  Lane 1
-// loads each phase's codebook (copy 0 of the table) and norm weights once
-// the consumers released the previous ones.
+// Producer warp: lane 0 streams the CTA's tasks through a ring of 16 KB
+// stages with bulk copies, in the order the warps consume them (rounds of
+// up to eight tasks, piece by piece).  Weights do not depend on
+// activations, so the stream runs ahead across phase boundaries.  Table
+// warp: bulk-copies each phase's codebook table (slot streams only) and
+// norm weights into one of two slots, two phases ahead.
 //
-// Consumers, per phase: build the codebook copies 1..R-1 in shared memory;
-// wait until every CTA finished the phase this one reads (a device-wide
-// counter, polled with a time limit); stage x in shared memory, chunk by
-// chunk (rmsnorm of the residual, the embedding row in layer 0, or a plain
-// vector: ctx, act).  GEMV task, lane = 8 * pair + chunk:
-//   rows   acc = fl(acc + fl(x[k] * cb[idx[k][n]])) over the chunk's rows in
+// Consumers, per phase: wait until every CTA finished the phase this one
+// reads (a device-wide counter, polled with a time limit); stage x in
+// shared memory, chunk by chunk (rmsnorm of the residual, the embedding row
+// in layer 0, or a plain vector: ctx, act).  GEMV task, lane = 8 * pair +
+// chunk, two columns per lane:
+//   rows   acc = fl(acc + fl(x[k] * w[k][n])) over the chunk's rows in
 //          order -- the reference's serial chunk sum (_tape_runner.c:530-545);
+//          w[k][n] is codebook[idx[k][n]], read from the stream's value
+//          pattern or gathered from the table;
 //   sum    chunk sums added in chunk order through shuffles
 //          (_tape_runner.c:646-662): every TT-GEMV result is bit-identical
-//          to the reference's;
+//          to the reference's (fast order: W partial sums in w order);
 //   out    RoPE + KV append (QKV), residual add (O, down), silu(gate) * up
 //          (gate_up), logits + first maximum (lm_head; the CTA that finishes
 //          last picks the token).
@@ -33,6 +36,8 @@
 // the consumers of every CTA leave at the next phase boundary together
 // (named barriers are never split).
 #pragma once
+
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -240,10 +245,43 @@ __device__ __forceinline__ DSVals ds_gather_step(const float *tab, const uint4 &
     return r;
 }
 
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float f16_lo(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+__device__ __forceinline__ float f16_hi(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+// The 8 (column 0, column 1) values of one step from its two stream words
+// per lane: table gathers (slot streams) or the patterns themselves.
+template <int VM>
+__device__ __forceinline__ DSVals ds_step_vals(const float *tab, const uint4 &q0, const uint4 &q1) {
+    if constexpr (VM == TTX_VSLOT) {
+        return ds_gather_step(tab, q0, q1);
+    } else {
+        const uint32_t a[4] = {q0.x, q0.y, q0.z, q0.w}, b[4] = {q1.x, q1.y, q1.z, q1.w};
+        DSVals r;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            if constexpr (VM == TTX_VBF16) {
+                r.v[2 * c] = make_float2(bf16_lo(a[c]), bf16_lo(b[c]));
+                r.v[2 * c + 1] = make_float2(bf16_hi(a[c]), bf16_hi(b[c]));
+            } else {
+                r.v[2 * c] = make_float2(f16_lo(a[c]), f16_lo(b[c]));
+                r.v[2 * c + 1] = make_float2(f16_hi(a[c]), f16_hi(b[c]));
+            }
+        }
+        return r;
+    }
+}
+
+template <int VM>
 __device__ __forceinline__ DSVals ds_load_step(const uint8_t *lp, const float *tab) {
     const uint4 q0 = *reinterpret_cast<const uint4 *>(lp);
     const uint4 q1 = *reinterpret_cast<const uint4 *>(lp + 512);
-    return ds_gather_step(tab, q0, q1);
+    return ds_step_vals<VM>(tab, q0, q1);
 }
 
 __device__ __forceinline__ float2 ds_mac_step(const float *xr, const DSVals &v, float2 acc) {
@@ -262,44 +300,48 @@ __device__ __forceinline__ float2 ds_mac_step(const float *xr, const DSVals &v, 
 // order.  Two register sets of two steps each: the codebook values of the
 // next two steps are in flight while the current two are multiplied and
 // added in row order.
+template <int VM>
 __device__ __forceinline__ float2 ds_steps_full(const uint8_t *pc, int lane, const float *xr,
                                                 int n, const float *tab, float2 acc) {
     const uint8_t *lp = pc + lane * 16;
     int i = 0;
     if (n >= 4) {
-        DSVals a0 = ds_load_step(lp, tab), a1 = ds_load_step(lp + TTX_STEP, tab);
+        DSVals a0 = ds_load_step<VM>(lp, tab), a1 = ds_load_step<VM>(lp + TTX_STEP, tab);
         for (; i + 4 <= n; i += 4) {
-            const DSVals b0 = ds_load_step(lp + (i + 2) * TTX_STEP, tab);
-            const DSVals b1 = ds_load_step(lp + (i + 3) * TTX_STEP, tab);
+            const DSVals b0 = ds_load_step<VM>(lp + (i + 2) * TTX_STEP, tab);
+            const DSVals b1 = ds_load_step<VM>(lp + (i + 3) * TTX_STEP, tab);
             acc = ds_mac_step(xr + 8 * i, a0, acc);
             acc = ds_mac_step(xr + 8 * i + 8, a1, acc);
             if (i + 6 <= n) {
-                a0 = ds_load_step(lp + (i + 4) * TTX_STEP, tab);
-                a1 = ds_load_step(lp + (i + 5) * TTX_STEP, tab);
+                a0 = ds_load_step<VM>(lp + (i + 4) * TTX_STEP, tab);
+                a1 = ds_load_step<VM>(lp + (i + 5) * TTX_STEP, tab);
             }
             acc = ds_mac_step(xr + 8 * i + 16, b0, acc);
             acc = ds_mac_step(xr + 8 * i + 24, b1, acc);
         }
     }
-    for (; i < n; i++) acc = ds_mac_step(xr + 8 * i, ds_load_step(lp + i * TTX_STEP, tab), acc);
+    for (; i < n; i++) acc = ds_mac_step(xr + 8 * i, ds_load_step<VM>(lp + i * TTX_STEP, tab), acc);
     return acc;
 }
 
 // One step of which only the first `rows` rows (< 8, may be <= 0) are in
 // the lane's chunk.
+template <int VM>
 __device__ __forceinline__ float2 ds_step_tail(const uint8_t *stp, int lane, const float *xr,
                                                int rows, const float *tab, float2 acc) {
     if (rows <= 0) return acc;
     const uint4 q0 = *reinterpret_cast<const uint4 *>(stp + lane * 16);
     const uint4 q1 = *reinterpret_cast<const uint4 *>(stp + 512 + lane * 16);
-    const DSVals v = ds_gather_step(tab, q0, q1);
+    const DSVals v = ds_step_vals<VM>(tab, q0, q1);
 #pragma unroll
     for (int e = 0; e < 8; e++)
         if (e < rows) acc = __fadd2_rn(acc, __fmul2_rn(make_float2(xr[e], xr[e]), v.v[e]));
     return acc;
 }
 
-template <int HD>
+// HD: head dim; VM: what the streams hold (TTXVals, the same for every
+// matrix of the step).
+template <int HD, int VM>
 __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_constant__ DSArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NQ = HD / 4;                 // float4 per head row
@@ -550,9 +592,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         const uint8_t *st = ring + (size_t)s * DS_STAGE;
                         const int s0 = DS_PIECE_STEPS * b, s1 = min(ns, s0 + DS_PIECE_STEPS);
                         const int sf = min(s1, max(s0, nfull));
-                        acc = ds_steps_full(st, lane, xr + 8 * s0, sf - s0, tab, acc);
+                        acc = ds_steps_full<VM>(st, lane, xr + 8 * s0, sf - s0, tab, acc);
                         for (int sg = sf; sg < s1; sg++)
-                            acc = ds_step_tail(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
+                            acc = ds_step_tail<VM>(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
                                                len - 8 * sg, tab, acc);
                     }
                     __syncwarp();

@@ -487,6 +487,7 @@ struct DecodePlan {
     // persistent step kernel
     bool persist = false;
     int order = 0;                 // KLLM_ORDER_* the layouts were built for
+    int vm = TTX_VSLOT;            // what the device streams hold (TTXVals)
     int ds_grid = 0, ds_stages = 0;
     size_t ds_smem = 0;
     DSArgs ds = {};
@@ -533,6 +534,12 @@ static void free_plan(DecodePlan *p) {
     delete p;
 }
 
+void plan_kind(const CtxImpl *c, int *persist, int *values) {
+    const DecodePlan *p = c->plan;
+    *persist = p && p->persist ? 1 : 0;
+    *values = p && p->persist ? p->vm : 0;
+}
+
 void plan_destroy(CtxImpl *c) {
     if (c->plan) {
         cudaSetDevice(c->device);
@@ -556,6 +563,19 @@ static bool env_on(const char *name, bool dflt) {
     return *v != '0';
 }
 
+typedef void (*DSKernel)(const DSArgs);
+
+template <int HD>
+static DSKernel ds_kernel_hd(int vm) {
+    return vm == TTX_VBF16 ? k_decode_step<HD, TTX_VBF16>
+         : vm == TTX_VF16  ? k_decode_step<HD, TTX_VF16>
+                           : k_decode_step<HD, TTX_VSLOT>;
+}
+
+static DSKernel ds_kernel(int hd, int vm) {
+    return hd == 32 ? ds_kernel_hd<32>(vm) : hd == 64 ? ds_kernel_hd<64>(vm) : ds_kernel_hd<128>(vm);
+}
+
 static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &tts) {
     if (!env_on("KLLM_PERSIST", true)) return false;
     const TapeCtx *ctx = &c->base;
@@ -565,7 +585,22 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     const int nmat = (int)tts.size();
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
-    auto kern = hd == 32 ? k_decode_step<32> : hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    // Value streams when every codebook holds only bf16 (or only fp16)
+    // numbers -- the compiler's codebooks of bf16 / fp16 checkpoints; table
+    // slots otherwise.  KLLM_TTX_VALUES=slot keeps the slot streams.
+    unsigned modes = (1u << TTX_VBF16) | (1u << TTX_VF16);
+    {
+        for (int ti : tts) {   // the host codebooks the device copies were made from
+            const Slot &sl = ctx->slots[ti];
+            modes &= ttx_value_modes(sl.codebook, sl.n_codes);
+            if (!modes) break;
+        }
+        const char *e = getenv("KLLM_TTX_VALUES");
+        if (e && !strcmp(e, "slot")) modes = 0;
+    }
+    const int vm = modes & (1u << TTX_VBF16) ? TTX_VBF16 : modes & (1u << TTX_VF16) ? TTX_VF16 : TTX_VSLOT;
+    p->vm = vm;
+    auto kern = ds_kernel(hd, vm);
     cudaFuncAttributes fa = {};
     if (!KLLM_CUDA(cudaFuncGetAttributes(&fa, kern))) return false;
     int smem_optin = 0;
@@ -598,16 +633,19 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
                    sl.tt_K % (16 * 8 * W) == 0)
                 W *= 2;
         }
-        if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, hd, t.nh + nkv, max_table, max_r, W,
-                          &desc[i]))
+        if (!ttx_describe(sl.tt_K, sl.tt_N, sl.n_codes, mode, vm, hd, t.nh + nkv, max_table, max_r,
+                          W, &desc[i]))
             return false;
         groups_all[i] = desc[i].ngroups;
         if (c->shard_world > 1) ttx_shard(&desc[i], c->shard_rank, c->shard_world);
         const TTXDesc &d = desc[i];
         if (!KLLM_CUDA(cudaMalloc((void **)&streams[i], d.stream_bytes()))) return false;
         own(streams[i]);
-        if (!KLLM_CUDA(cudaMalloc((void **)&tables[i], d.table_elems() * 4))) return false;
-        own(tables[i]);
+        tables[i] = nullptr;
+        if (d.table_elems()) {
+            if (!KLLM_CUDA(cudaMalloc((void **)&tables[i], d.table_elems() * 4))) return false;
+            own(tables[i]);
+        }
         if (!ttx_build(c->stream, w.d_idx, w.d_cb, d, streams[i], tables[i])) return false;
         tab_cap = std::max(tab_cap, (int)d.table_elems());
         // staged x: chunk rows of 8 * ns floats, padded to 4 mod 32 floats so
@@ -855,12 +893,6 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         *why = "head_dim " + std::to_string(ti.hd) + " (fused attention covers 32, 64, 128)";
         return false;
     }
-    if (ti.F % 8 != 0) {
-        // the up half of each gate_up tile starts at column F: a TMA x
-        // coordinate must be a multiple of 8 uint16
-        *why = "intermediate size not a multiple of 8";
-        return false;
-    }
     if ((size_t)max_pos * 4 > 160 * 1024) {
         *why = "context longer than the fused attention's score buffer";
         return false;
@@ -900,6 +932,9 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         const Slot &sl = ctx->slots[s];
         (void)sl;
     }
+    // The per-kernel plan (fallback of the persistent step) reads the
+    // index matrices by TMA tiles; the persistent step needs neither.
+    std::string tf_why;
     p->maps.resize(tts.size());
     p->cfgs.resize(tts.size());
     for (size_t i = 0; i < tts.size(); i++) {
@@ -907,11 +942,14 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         const int em = (i + 1 == tts.size()) ? E_ARGMAX : (i % 4 == 2 ? E_SWIGLU : E_Y);
         p->cfgs[i] = tf_config(sl.tt_K, sl.tt_N, sl.n_codes, em);
         if (!tf_tma_ok(c->ds[tts[i]].d_idx, c->ds[tts[i]].d_cb, sl.tt_K, sl.tt_N, sl.n_codes,
-                       p->cfgs[i])) {
-            *why = "a weight matrix does not meet the TMA alignment rules";
-            free_plan(p);
-            return false;
-        }
+                       p->cfgs[i]))
+            tf_why = "a weight matrix does not meet the TMA alignment rules";
+    }
+    // the up half of each gate_up tile starts at column F: a TMA x
+    // coordinate must be a multiple of 8 uint16
+    if (F % 8) tf_why = "intermediate size not a multiple of 8";
+    for (size_t i = 0; i < tts.size() && tf_why.empty(); i++) {
+        const Slot &sl = ctx->slots[tts[i]];
         if (!make_idx_tmap(&p->maps[i], c->ds[tts[i]].d_idx, sl.tt_K, sl.tt_N,
                            p->cfgs[i].bw(), 32))
             return fail();
@@ -959,11 +997,7 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         const int em = (i + 1 == tts.size()) ? E_ARGMAX : (i % 4 == 2 ? E_SWIGLU : E_Y);
         nblk = std::max(nblk, tf_blocks(p->cfgs[i], sl.tt_N, sl.tt_N / 2, em));
     }
-    if (nblk > 1024 || nblk > n_cnt) {
-        *why = "too many column blocks for the argmax candidates";
-        free_plan(p);
-        return false;
-    }
+    if (nblk > 1024 || nblk > n_cnt) tf_why = "too many column blocks for the argmax candidates";
     if (!dalloc(&p->h, H) || !dalloc(&p->qkv, nq) || !dalloc(&p->ctx, qd) ||
         !dalloc(&p->act, F) || !dalloc(&p->logits, V) || !dalloc(&p->part, part_n) ||
         !dalloc(&p->counters, n_cnt) || !dalloc(&p->kc, kv) || !dalloc(&p->vc, kv) ||
@@ -982,8 +1016,17 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why) 
         !KLLM_CUDA(cudaEventCreate(&p->ev2)))
         return fail();
     if (!persist_prepare(c, p, tts)) {
-        kllm_clear_error();   // the per-kernel plan remains available
+        // the per-kernel plan remains available; KLLM_VERBOSE=1 says why
+        if (env_on("KLLM_VERBOSE", false))
+            fprintf(stderr, "kllm: persistent decode step unavailable: %s\n",
+                    kllm_last_error() ? kllm_last_error() : "shape or resource limit");
+        kllm_clear_error();
         p->persist = false;
+        if (!tf_why.empty()) {
+            *why = tf_why;
+            free_plan(p);
+            return false;
+        }
     }
     c->plan = p;
     return true;
@@ -1028,8 +1071,7 @@ static bool record_step_persist(CtxImpl *c, DecodePlan *p) {
     DSArgs a = p->ds;
     a.hist = p->hist;
     a.hist_rows = p->hist_rows;
-    auto kern = p->ti.hd == 32 ? k_decode_step<32>
-                               : p->ti.hd == 64 ? k_decode_step<64> : k_decode_step<128>;
+    auto kern = ds_kernel(p->ti.hd, p->vm);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p->ds_grid);
     cfg.blockDim = dim3(DS_THREADS);

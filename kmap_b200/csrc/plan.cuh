@@ -30,6 +30,10 @@ bool plan_prepare(CtxImpl *c, const PlanDesc &d, int max_pos, std::string *why);
 bool plan_shard_export(CtxImpl *c, void *out, size_t cap, size_t *len);
 bool plan_shard_connect(CtxImpl *c, const void *all, size_t per_rank);
 
+// Which step kernel the plan runs (persistent: 1) and what its weight
+// streams hold (TTXVals); zeros without a plan.
+void plan_kind(const CtxImpl *c, int *persist, int *values);
+
 // Prefill + greedy decode on the plan.  emit(token, i) is called for every
 // generated token in order and returns false to stop.
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,

@@ -2,11 +2,31 @@
 // (column-group slot stream + bank-spread replicated codebook); see ttx.cuh.
 #include "ttx.cuh"
 
+#include <cuda_fp16.h>
+#include <string.h>
+
 namespace kllm {
 
-bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads,
+unsigned ttx_value_modes(const float *cb, int n_codes) {
+    bool bf = true, hf = true;
+    for (int i = 0; i < n_codes && (bf || hf); i++) {
+        uint32_t u;
+        memcpy(&u, cb + i, 4);
+        if (u & 0xffffu) bf = false;
+        if (hf) {
+            const float back = __half2float(__float2half_rn(cb[i]));
+            uint32_t v;
+            memcpy(&v, &back, 4);
+            if (v != u) hf = false;
+        }
+    }
+    return (bf ? 1u << TTX_VBF16 : 0u) | (hf ? 1u << TTX_VF16 : 0u);
+}
+
+bool ttx_describe(int K, int N, int n_codes, int colmode, int vmode, int hd, int rope_heads,
                   int max_table_bytes, int max_r, int split_w, TTXDesc *d) {
     if (K <= 0 || N <= 0 || n_codes <= 0) return false;
+    if (vmode != TTX_VSLOT && vmode != TTX_VBF16 && vmode != TTX_VF16) return false;
     if (split_w != 1 && split_w != 2 && split_w != 4 && split_w != 8) return false;
     TTXDesc t = {};
     t.K = K;
@@ -35,7 +55,13 @@ bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads
     }
     t.gstride = 1;
     t.goff = 0;
+    t.vmode = vmode;
     t.npad = (n_codes + 31) & ~31;
+    if (vmode != TTX_VSLOT) {   // values in the stream: no table
+        t.R = 0;
+        *d = t;
+        return true;
+    }
     // slots are byte offsets into the table: R * npad * 4 must fit 16 bits
     int r = 4;
     while (r > max_r || (r > 1 && ((size_t)r * t.npad * 4 > (size_t)max_table_bytes ||
@@ -55,12 +81,13 @@ void ttx_shard(TTXDesc *d, int rank, int world) {
 
 // One thread per warp-wide gather of the decode kernel: group g, sub-task w,
 // step s, column half k, row e -- lane l = 8 * pair + c reads column
-// 2 * pair + k, row 8s + e of chunk 8w + c.  It chooses a codebook copy for
-// every distinct code so that the bank holding the most distinct words holds
-// as few as possible.  Exact: for cap = 1, 2, ... every code is inserted with
-// a breadth-first augmenting path over banks (a bank may hold cap words).
-__global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
-                            uint8_t *__restrict__ out, long long ngather) {
+// 2 * pair + k, row 8s + e of chunk 8w + c.  Value streams store the code's
+// bf16 / fp16 pattern.  Slot streams choose a codebook copy for every
+// distinct code so that the bank holding the most distinct words holds as
+// few as possible.  Exact: for cap = 1, 2, ... every code is inserted with a
+// breadth-first augmenting path over banks (a bank may hold cap words).
+__global__ void k_ttx_build(const uint16_t *__restrict__ idx, const float *__restrict__ cb,
+                            const TTXDesc d, uint8_t *__restrict__ out, long long ngather) {
     const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (gid >= ngather) return;
     const int e = (int)(gid & 7), k = (int)((gid >> 3) & 1);
@@ -69,6 +96,23 @@ __global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
     const long long gw = gs / d.ns;          // i * W + w, i a stored group
     const int g = (int)(gw / d.W) * d.gstride + d.goff, w = (int)(gw % d.W);
 
+    uint16_t *step = reinterpret_cast<uint16_t *>(out + ((size_t)gw * d.ns + s) * TTX_STEP);
+    if (d.vmode != TTX_VSLOT) {
+        for (int l = 0; l < 32; l++) {
+            const int t = 8 * w + (l & 7), pair = l >> 3;
+            const int row = 8 * s + e;
+            const int n = ttx_col(d, g, 2 * pair + k);
+            uint16_t v = 0;   // rows past the chunk and padding columns are never used
+            if (row < d.chunk_len(t) && n >= 0) {
+                int c = idx[((size_t)d.chunk_start(t) + row) * d.N + n];
+                if (c >= d.n_codes) c = 0;   // indices are validated at upload
+                v = d.vmode == TTX_VBF16 ? (uint16_t)(__float_as_uint(cb[c]) >> 16)
+                                         : __half_as_ushort(__float2half_rn(cb[c]));
+            }
+            step[k * 256 + l * 8 + e] = v;
+        }
+        return;
+    }
     int code[32];   // distinct codes
     int lane_u[32];
     int nu = 0;
@@ -147,7 +191,6 @@ __global__ void k_ttx_build(const uint16_t *__restrict__ idx, const TTXDesc d,
             fill = 4 * (copy[u] * d.npad + ttx_swz(code[u], copy[u]));
             break;
         }
-    uint16_t *step = reinterpret_cast<uint16_t *>(out + ((size_t)gw * d.ns + s) * TTX_STEP);
     for (int l = 0; l < 32; l++) {
         const int u = lane_u[l];
         const int slot = u >= 0 ? 4 * (copy[u] * d.npad + ttx_swz(code[u], copy[u])) : fill;
@@ -169,9 +212,9 @@ bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDe
     if (ngather < 0) return false;
     if (ngather == 0) return true;   // a rank without groups of this matrix
     const int bs = 128;
-    k_ttx_build<<<(unsigned)((ngather + bs - 1) / bs), bs, 0, s>>>(idx, d, stream, ngather);
+    k_ttx_build<<<(unsigned)((ngather + bs - 1) / bs), bs, 0, s>>>(idx, cb, d, stream, ngather);
     if (!KLLM_CUDA(cudaGetLastError())) return false;
-    if (!table) return true;
+    if (!table || d.table_elems() == 0) return true;
     k_ttx_table<<<64, 256, 0, s>>>(cb, d, table);
     return KLLM_CUDA(cudaGetLastError());
 }

@@ -22,6 +22,12 @@
 //    holds as few distinct words as possible (an exact bipartite
 //    assignment with bank capacities).  The values read are the codebook
 //    entries themselves, so products and sums are unchanged bit for bit.
+//  * Value streams.  When every codebook entry is a bf16 (or fp16) number --
+//    the usual case: the compiler's codebook is the sorted distinct values
+//    of a bf16 (fp16) checkpoint -- the stream holds each weight's 16-bit
+//    pattern instead of a table slot, still 2 bytes a weight.  Converting
+//    the pattern to float gives the codebook entry exactly, so products and
+//    sums are unchanged bit for bit, and no table or gather is needed.
 //  * Split groups (decode's fast order).  With W > 1 a group's K is cut into
 //    8W equal chunks instead of the reference's T: sub-task w of the group
 //    (its own NS steps, lane chunk 8w + lane % 8) goes to its own warp, and
@@ -44,6 +50,9 @@ constexpr int TTX_STEP = 1024;   // bytes per step of a column group
 constexpr int TTX_GCOLS = 8;     // columns per group
 
 enum TTXCols : int { TTX_IDENT = 0, TTX_GATE_UP = 1, TTX_ROPE = 2 };
+// What a stream holds per weight: a table slot, or the value's bf16 / fp16
+// pattern (exact codebooks only).
+enum TTXVals : int { TTX_VSLOT = 0, TTX_VBF16 = 1, TTX_VF16 = 2 };
 
 struct TTXDesc {
     int K, N, n_codes;
@@ -52,8 +61,10 @@ struct TTXDesc {
     int ns;               // steps per group (8 rows of every chunk per step)
     int ngroups;          // groups stored here (a column shard: every gstride-th)
     int gstride, goff;    // stored group i is group i * gstride + goff of the matrix
-    int R, npad;          // codebook copies, entries per copy (multiple of 32)
+    int R, npad;          // codebook copies, entries per copy (multiple of 32); R = 0
+                          // for value streams (no table)
     int colmode;
+    int vmode;            // TTXVals
     int F;                // TTX_GATE_UP: N == 2F
     int hd, rope_heads;   // TTX_ROPE: head dim, q + k heads (rotated)
     __host__ __device__ size_t stream_bytes() const {
@@ -94,17 +105,22 @@ __host__ __device__ inline int ttx_col(const TTXDesc &d, int g, int c) {
     return n < d.N ? n : -1;
 }
 
-// Fill in the layout of a K x N matrix with n_codes codes.  R is the largest
-// of 4, 2, 1 (at most max_r) whose table fits max_table_bytes and whose
-// slots fit 16 bits.  TTX_ROPE needs hd (a multiple of 8) and the number
-// of rotated heads.  split_w = 1 keeps the reference's chunks; 2, 4 or 8
-// splits each group into that many sub-tasks (fast order).
-bool ttx_describe(int K, int N, int n_codes, int colmode, int hd, int rope_heads,
+// Fill in the layout of a K x N matrix with n_codes codes.  For slot
+// streams R is the largest of 4, 2, 1 (at most max_r) whose table fits
+// max_table_bytes and whose slots fit 16 bits.  TTX_ROPE needs hd (a
+// multiple of 8) and the number of rotated heads.  split_w = 1 keeps the
+// reference's chunks; 2, 4 or 8 splits each group into that many sub-tasks
+// (fast order).
+bool ttx_describe(int K, int N, int n_codes, int colmode, int vmode, int hd, int rope_heads,
                   int max_table_bytes, int max_r, int split_w, TTXDesc *d);
+// The value streams a codebook allows: bit TTX_VBF16 set when every entry
+// is a bf16 number, bit TTX_VF16 when every entry is an fp16 number (bit
+// patterns compared, so -0.0 and NaN payloads must survive the round trip).
+unsigned ttx_value_modes(const float *cb, int n_codes);
 // Restrict d to the column groups of one rank (group g with g % world == rank).
 void ttx_shard(TTXDesc *d, int rank, int world);
-// Build the slot stream and (table != nullptr) the replicated table on the
-// device.
+// Build the stream and (slot streams, table != nullptr) the replicated
+// table on the device.
 bool ttx_build(cudaStream_t s, const uint16_t *idx, const float *cb, const TTXDesc &d,
                uint8_t *stream, float *table);
 

@@ -60,7 +60,19 @@ TINY_SPECS = {
     # TinyLlama's head geometry (hd 64, 8 q heads per kv head) at a small width
     "tl": dict(num_layers=2, hidden_size=512, num_attention_heads=8, num_key_value_heads=1,
                intermediate_size=1408, vocab_size=2048, max_seq=160, seed=7),
+    # the same with fp16 weights (fp16 value streams) and with 4096-value fp32
+    # codebooks (neither bf16 nor fp16: codebook-table streams)
+    "tl-fp16": dict(num_layers=2, hidden_size=512, num_attention_heads=8, num_key_value_heads=1,
+                    intermediate_size=1408, vocab_size=2048, max_seq=160, seed=7,
+                    weight_values="fp16"),
+    "tl-pool": dict(num_layers=2, hidden_size=512, num_attention_heads=8, num_key_value_heads=1,
+                    intermediate_size=1408, vocab_size=2048, max_seq=160, seed=7,
+                    weight_values="pool4096"),
 }
+
+#: what the persistent step's weight streams hold for each tiny chip
+#: (kllm_infer_stats.stream_values: 0 table slots, 1 bf16, 2 fp16)
+TINY_STREAM_VALUES = {"gqa": 1, "mha": 1, "tl": 1, "tl-fp16": 2, "tl-pool": 0}
 
 
 @pytest.fixture(scope="session")

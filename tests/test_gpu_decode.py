@@ -20,10 +20,11 @@ def _oracle_run(oracle, path, prompt, max_new):
     return toks, lg
 
 
-@pytest.mark.parametrize("name", ["gqa", "mha", "tl"])
+@pytest.mark.parametrize("name", ["gqa", "mha", "tl", "tl-fp16", "tl-pool"])
 @pytest.mark.parametrize("mode", ["generic", "auto", "auto-fast"])
 def test_tiny_chip_tokens_and_logits(gpu, oracle, chip_dir, name, mode):
     import kmap_b200
+    from conftest import TINY_STREAM_VALUES
     path = chip_dir(name)
     order = kmap_b200.ORDER_FAST if mode == "auto-fast" else kmap_b200.ORDER_EXACT
     with kmap_b200.Chip(path, order=order) as chip:
@@ -33,8 +34,30 @@ def test_tiny_chip_tokens_and_logits(gpu, oracle, chip_dir, name, mode):
         toks_o, lg_o = _oracle_run(oracle, path, prompt, max_new)
         m = kmap_b200.MODE_GENERIC if mode == "generic" else kmap_b200.MODE_AUTO
         toks_g, lg_g = chip.infer(prompt, max_new, mode=m, logits=True)
+        st = chip.stats()
+        if mode != "generic":
+            assert st["fused"] == 1 and st["step_kernel"] == 1
+            assert st["stream_values"] == TINY_STREAM_VALUES[name]
         assert toks_g.tolist() == toks_o.tolist()
         np.testing.assert_allclose(lg_g, lg_o, rtol=RTOL, atol=ATOL)
+
+
+def test_slot_streams_forced_match_value_streams(gpu, chip_dir, monkeypatch):
+    """A bf16 chip run with codebook-table streams (KLLM_TTX_VALUES=slot)
+    gives the same bits as with bf16 value streams: both read the codebook
+    entries themselves."""
+    import kmap_b200
+    path = chip_dir("tl")
+    prompt = np.random.default_rng(5).integers(3, 2048, 5)
+    with kmap_b200.Chip(path) as chip:
+        t1, l1 = chip.infer(prompt, 10, logits=True)
+        assert chip.stats()["stream_values"] == 1
+    monkeypatch.setenv("KLLM_TTX_VALUES", "slot")
+    with kmap_b200.Chip(path) as chip:
+        t2, l2 = chip.infer(prompt, 10, logits=True)
+        assert chip.stats()["step_kernel"] == 1 and chip.stats()["stream_values"] == 0
+    assert t1.tolist() == t2.tolist()
+    assert np.array_equal(l1.view(np.uint32), l2.view(np.uint32))
 
 
 def test_eos_stops_generation(gpu, oracle, chip_dir):
@@ -83,17 +106,20 @@ def test_infer_bytes_matches_reference(gpu, ref, chip_dir):
         assert gen_s == 3 and out_s == b"".join(pieces[:3])
 
 
-@pytest.mark.parametrize("order", ["exact", "fast"])
-def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path, order):
+@pytest.mark.parametrize("order,values", [("exact", "bf16"), ("fast", "bf16"),
+                                          ("exact", "fp16"), ("exact", "pool4096")])
+def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path, order, values):
     """Two layers at the TinyLlama-1.1B widths (K = 2048 and 5632, N up to
     32000, eight K-chunks per column): the fused step kernel's real tile,
-    ring and codebook-table geometry, against the compiled reference
-    runtime on the same chip."""
+    ring and stream geometry (bf16 / fp16 value streams, codebook tables
+    for the 4096-value pools), against the compiled reference runtime on
+    the same chip."""
     import kmap_b200
     from kmap_b200 import chipgen
     spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
     spec.num_layers = 2
     spec.max_seq = 256
+    spec.weight_values = values
     path = chipgen.ensure_chip(str(tmp_path), spec)
     prompt = np.random.default_rng(3).integers(3, spec.vocab_size, 6).astype(np.int32)
     max_new = 6
@@ -103,7 +129,8 @@ def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path, order):
     o = kmap_b200.ORDER_FAST if order == "fast" else kmap_b200.ORDER_EXACT
     with kmap_b200.Chip(path, order=o) as chip:
         toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
-        assert chip.stats()["fused"] == 1
+        assert chip.stats()["fused"] == 1 and chip.stats()["step_kernel"] == 1
+        assert chip.stats()["stream_values"] == {"bf16": 1, "fp16": 2, "pool4096": 0}[values]
     assert toks_g.tolist() == toks_r.tolist()
     n = len(prompt) + max_new - 1   # the last step's logits are not computed
     np.testing.assert_allclose(lg_g[:n], lg_r[:n], rtol=RTOL, atol=ATOL)
