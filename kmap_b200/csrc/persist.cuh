@@ -48,17 +48,23 @@ namespace kllm {
 
 enum DSKind : int { DS_GEMV = 0, DS_ATT = 1 };
 // Buffers every rank of a column-sharded decode holds a full copy of; a rank
-// stores its columns' results into all copies (DSArgs::peers).
+// stores its columns' results into all copies (DSArgs::peers).  Q, HA, HB,
+// ACT, KN and VN hold tagged words (ll_t).
 enum DSPeer : int {
     DSP_Q = 0, DSP_KC, DSP_VC, DSP_HA, DSP_HB, DSP_ACT, DSP_LOGITS, DSP_CANDV, DSP_CANDI,
-    DSP_DONE, DSP_KINDS
+    DSP_KN, DSP_VN, DSP_DONE, DSP_KINDS
 };
+
+// An activation word: the float's bits in the low half, the tag of the
+// (step, layer) that wrote it in the high half, stored and loaded as one
+// 8-byte access.  A reader that sees its tag sees the value: waiting for an
+// input and reading it are one poll, with no counter, fence or second load.
+typedef unsigned long long ll_t;
 enum DSX : int { DX_EMBED = 0, DX_NORM = 1, DX_VEC = 2 };
 enum DSE : int { DE_QKV = 0, DE_RESID = 1, DE_SWIGLU = 2, DE_LM = 3 };
 
 struct DSPhase {
     int kind, ntasks;          // GEMV: column groups; attention: heads
-    int dep, dep_count;        // wait for done[dep] >= dep_count per step (dep < 0: none)
     TTXDesc d;                 // GEMV layout (ttx.cuh)
     int npieces;               // 16-step pieces per group
     int xs;                    // floats per chunk row of the staged x
@@ -67,12 +73,13 @@ struct DSPhase {
     const float *table;        // replicated codebook table (ttx.cuh), built at upload
     int table_bytes;
     int xmode, emode;
-    const float *x;            // DX_NORM: residual; DX_VEC: input vector
+    const ll_t *x;             // DX_NORM: residual; DX_VEC: input vector (tagged words)
     const float *norm_w;
     float eps;
-    const float *hold;         // DE_RESID: residual in (nullptr: embedding row)
-    float *out;                // q / new residual / act / logits (this rank's copy)
-    int out_kind;              // DSPeer of out
+    int x_layer;               // the layer whose tag x carries
+    int save_x;                // keep the raw x: the residual of a later epilogue
+    float *out;                // logits (DE_LM, this rank's copy)
+    int out_kind;              // DSPeer of the output
     int groups_all;            // column groups of the matrix over all ranks
     int layer;
 };
@@ -94,12 +101,12 @@ struct DSArgs {
     volatile int *gen_host;
     int vocab, max_gen, H;
     // attention
-    float *q;
+    const ll_t *q;             // this rank's copy
     int nh, nkv, groups, max_pos, qd, kvd;
     const float *rope_cos, *rope_sin;
     float *kc, *vc;            // [L][nkv][max_pos][hd]
     float scale;
-    float *ctx;
+    ll_t *ctx;
     // lm_head
     float *hist;
     int hist_rows;
@@ -119,6 +126,27 @@ __device__ __forceinline__ T *ds_peer(const DSArgs &a, int kind, int r) {
 // Store v at index i of every rank's copy of buffer `kind`.
 __device__ __forceinline__ void ds_put(const DSArgs &a, int kind, size_t i, float v) {
     for (int r = 0; r < a.world; r++) ds_peer<float>(a, kind, r)[i] = v;
+}
+
+__device__ __forceinline__ uint32_t ds_tag(int ep1, int layer) {
+    return (uint32_t)ep1 * 256u + (uint32_t)layer;
+}
+
+__device__ __forceinline__ void st_ll(ll_t *p, float v, uint32_t tag) {
+    const ll_t w = ((ll_t)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ ll_t ld_ll(const ll_t *p) {
+    ll_t w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Store v with its tag at index i of every rank's copy of buffer `kind`.
+__device__ __forceinline__ void ds_put_ll(const DSArgs &a, int kind, size_t i, float v,
+                                          uint32_t tag) {
+    for (int r = 0; r < a.world; r++) st_ll(ds_peer<ll_t>(a, kind, r) + i, v, tag);
 }
 
 // CTAs of rank r with work in a phase of `groups_all` column groups.
@@ -187,6 +215,61 @@ __device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *sta
         }
         __nanosleep(32);
     }
+    return true;
+}
+
+// Give up a poll: record the timeout and raise the abort flag.
+__device__ __forceinline__ bool ds_poll_expired(unsigned long long &t0, const DSArgs &a) {
+    const unsigned long long now = globaltimer();
+    if (!t0) t0 = now;
+    if (now - t0 <= kWaitLimitNs) return false;
+    atomicOr(a.status, ST_WAIT_TIMEOUT);
+    atomicExch(a.abort, 1);
+    return true;
+}
+
+constexpr int LL_BATCH = 16;   // words in flight per thread
+
+// Read n (<= LL_BATCH) activation words src[32 u], u < n, written with
+// `tag`: one batch of loads, then batches of reloads of the words not
+// written yet.  False when the wait ran out or another CTA aborted.
+__device__ __forceinline__ bool ll_fetch(const ll_t *src, int n, uint32_t tag,
+                                         float (&out)[LL_BATCH], const DSArgs &a) {
+    ll_t w[LL_BATCH];
+    unsigned pend = 0;
+#pragma unroll
+    for (int u = 0; u < LL_BATCH; u++) {
+        w[u] = u < n ? ld_ll(src + 32 * u) : 0ull;
+        if (u < n) pend |= 1u << u;
+    }
+    unsigned long long t0 = 0;
+    for (;;) {
+#pragma unroll
+        for (int u = 0; u < LL_BATCH; u++)
+            if ((uint32_t)(w[u] >> 32) == tag) pend &= ~(1u << u);
+        if (!pend) break;
+        __nanosleep(32);
+#pragma unroll
+        for (int u = 0; u < LL_BATCH; u++)
+            if (pend >> u & 1u) w[u] = ld_ll(src + 32 * u);
+        if (ld_acquire(a.abort) || ds_poll_expired(t0, a)) return false;
+    }
+#pragma unroll
+    for (int u = 0; u < LL_BATCH; u++) out[u] = __uint_as_float((uint32_t)w[u]);
+    return true;
+}
+
+// One activation word written with `tag`.
+__device__ __forceinline__ bool ll_fetch1(const ll_t *src, uint32_t tag, float *out,
+                                          const DSArgs &a) {
+    ll_t w = ld_ll(src);
+    unsigned long long t0 = 0;
+    while ((uint32_t)(w >> 32) != tag) {
+        __nanosleep(32);
+        w = ld_ll(src);
+        if (ld_acquire(a.abort) || ds_poll_expired(t0, a)) return false;
+    }
+    *out = __uint_as_float((uint32_t)w);
     return true;
 }
 
@@ -348,8 +431,10 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     constexpr int NPG = DS_NC / NQ;            // position groups in P.V
     __shared__ float red[DS_NCW + 1];
     __shared__ __align__(16) float qv[HD];
+    __shared__ __align__(16) float knv[2][HD];   // this position's k and v (attention)
     __shared__ __align__(16) float pctx[NPG][HD];
-    __shared__ int s_flag, s_tok;
+    __shared__ float rcs[2][HD];               // RoPE cos / sin of this position
+    __shared__ int s_bad;                      // a consumer warp gave up a wait
     __shared__ int ri[DS_NCW];
     __shared__ float2 sub_y[DS_NCW][4];        // split groups: each warp's column sums
 
@@ -361,7 +446,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     float *wns = tabs + 2 * a.tab_cap; // 2 phases' norm weights
     float *xc = wns + 2 * a.wn_cap;    // staged x, chunk-major
     float *sc = xc;                    // attention scores (no GEMV then)
-    uint64_t *full = reinterpret_cast<uint64_t *>(xc + a.xc_cap);
+    float *hsave = xc + a.xc_cap;      // raw x of QKV / gate_up: the residual of O / down
+    uint64_t *full = reinterpret_cast<uint64_t *>(hsave + a.wn_cap);
     uint64_t *empty = full + S;
     uint64_t *tready = empty + S;      // [2] table built
     uint64_t *tfree = tready + 2;      // [2] table no longer read
@@ -383,6 +469,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         }
         mbar_init(rawfull, 1);
         mbar_fence_init();
+        s_bad = 0;
     }
     __syncthreads();
 
@@ -462,47 +549,32 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     // =============================================================== consumers
     const int tid = threadIdx.x;
     const int t = lane & 7, cp = lane >> 3;    // chunk, column pair
-    // The arrival counters are never reset between steps: this step's
-    // targets are (epoch + 1) times a phase's per-step count.
+    // This step's number: the tag of every activation word written in it,
+    // and (times a phase's arrivals) the lm_head counter's target.
     const int ep1 = *a.epoch + 1;
+    const int pos = a.st->pos;
+    if (pos < a.max_pos)   // read by the QKV epilogues, after the first barrier
+        for (int d = tid; d < HD; d += DS_NC) {
+            rcs[0][d] = __ldg(a.rope_cos + (size_t)pos * HD + d);
+            rcs[1][d] = __ldg(a.rope_sin + (size_t)pos * HD + d);
+        }
     int seq_base = 0, q = 0;
     float lm_v = -INFINITY;                    // this warp's first maximum
     int lm_i = -1;
+    bool bad = false;                          // this warp gave up a wait
     for (int p = 0; p < a.nphases; p++) {
         const DSPhase &ph = a.phases[p];
         if (cta >= ph.ntasks) continue;
-        bool bad = false;
-        if (tid == 0) {
-            bool ok = !ld_acquire(a.abort);
-            if (ok && ph.dep >= 0)
-                ok = ds_wait_counter(a.done + ph.dep, ph.dep_count * ep1, a.status, a.abort);
-            s_flag = ok ? 1 : 0;
-        }
-        cbar_sync();
-        if (!s_flag) break;   // uniform: every consumer warp leaves together
+        const uint32_t otag = ds_tag(ep1, ph.layer);
         if (ph.kind == DS_GEMV) {
             const TTXDesc &d = ph.d;
             const int K = d.K, xs = ph.xs, xmode = ph.xmode;
             // ------------------------------------------------ stage x
-            const float *src = ph.x;
-            if (xmode == DX_EMBED) {
-                if (tid == 0) {
-                    int tok = ds_token(a);
-                    if (tok < 0) {
-                        atomicOr(a.status, ST_BAD_TOKEN);
-                        tok = 0;
-                    }
-                    s_tok = tok;
-                }
-                cbar_sync();
-                src = a.embed + (size_t)s_tok * K;
-            }
             // Warp w stages its rows of x -- chunk w (reference order,
             // T <= 8) or chunks W*w .. W*w + W - 1 (fast order: equal chunks
             // of L rows, one contiguous range) -- then rmsnorm in place:
-            // x * rsqrt(mean(x^2) + eps) * w.  Compact loops: this runs once
-            // per phase and must not crowd the task loop out of the
-            // instruction cache.
+            // x * rsqrt(mean(x^2) + eps) * w.  Tagged inputs are polled:
+            // the wait for the producing phase and the read are one.
             const bool norm = xmode != DX_VEC;
             const int CH = (d.T + DS_NCW - 1) / DS_NCW;   // chunks per warp
             const int wrows = CH == 1 ? (warp < d.T ? d.chunk_len(warp) : 0) : CH * d.base;
@@ -512,23 +584,45 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 const int cq = CH == 1 ? 0 : (int)__umulhi((unsigned)r, ph.lmagic);
                 return (CH * warp + cq) * xs + (r - cq * d.base);
             };
+            const float *emb = nullptr;
+            if (xmode == DX_EMBED) {
+                int tok = lane == 0 ? ds_token(a) : 0;
+                tok = __shfl_sync(0xffffffffu, tok, 0);
+                if (tok < 0) {
+                    if (lane == 0) atomicOr(a.status, ST_BAD_TOKEN);
+                    tok = 0;
+                }
+                emb = a.embed + (size_t)tok * K;
+            }
+            const uint32_t xtag = ds_tag(ep1, ph.x_layer);
             float ss = 0.f;
-            for (int r0 = lane; r0 < wrows; r0 += 8 * 32) {
-                float v[8];
+            for (int b0 = 0; b0 < wrows; b0 += 32 * LL_BATCH) {
+                float v[LL_BATCH];
+                const int nu = min(LL_BATCH, (wrows - b0 - lane + 31) / 32);   // rows b0 + lane + 32u
+                if (emb) {
 #pragma unroll
-                for (int u = 0; u < 8; u++)
-                    v[u] = r0 + 32 * u < wrows ? __ldcg(src + wk0 + r0 + 32 * u) : 0.f;
+                    for (int u = 0; u < LL_BATCH; u++)
+                        v[u] = u < nu ? __ldcg(emb + wk0 + b0 + lane + 32 * u) : 0.f;
+                } else if (!bad && !ll_fetch(ph.x + wk0 + b0 + lane, nu, xtag, v, a)) {
+                    bad = true;
+                }
+                if (bad) continue;
 #pragma unroll
-                for (int u = 0; u < 8; u++)
-                    if (r0 + 32 * u < wrows) {
-                        xc[slot_of(r0 + 32 * u)] = v[u];
+                for (int u = 0; u < LL_BATCH; u++)
+                    if (u < nu) {
+                        const int r = b0 + lane + 32 * u;
+                        xc[slot_of(r)] = v[u];
                         ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
+                        if (ph.save_x) hsave[wk0 + r] = v[u];
                     }
             }
             const int slot = q & 1;
             const float *tab = tabs + slot * a.tab_cap;
-            bad = !mbar_wait(&tready[slot], (q >> 1) & 1, a.status);
-            if (bad) atomicExch(a.abort, 1);
+            if (!bad && !mbar_wait(&tready[slot], (q >> 1) & 1, a.status)) {
+                bad = true;
+                atomicExch(a.abort, 1);
+            }
+            if (bad) s_bad = 1;
             if (norm) {
                 const float *wn = wns + slot * a.wn_cap;   // staged with the table
                 const float tot = ds_block_sum(ss, red);
@@ -540,11 +634,11 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
             }
             cbar_sync();
+            if (s_bad) break;   // uniform: every consumer warp leaves together
             // ------------------------------------------------ tasks
             const int W = d.W;
             const int J = (ph.ntasks - cta + G - 1) / G * W, ns = d.ns, np = ph.npieces;
             const int nfull = d.base / 8;             // steps inside every chunk
-            const int pos = a.st->pos;
             // warp task j: sub-task w = j % W of group m = j / W; a group's W
             // sub-tasks sit on W adjacent warps of one round
             for (int j = warp; j < J; j += DS_NCW) {
@@ -556,29 +650,6 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 const float *xr = ch < d.T ? xc + ch * xs : xc;
                 const int nch = min(DS_NCW, d.T - DS_NCW * w);   // chunks in this sub-task
                 const int n0 = ttx_col(d, g, 2 * cp), n1 = ttx_col(d, g, 2 * cp + 1);
-                // the epilogue's operands, fetched while the task computes
-                float2 ea = make_float2(0.f, 0.f), eb = make_float2(0.f, 0.f);
-                if (t == 0 && w == 0) {
-                    if (ph.emode == DE_RESID) {
-                        const float *h = ph.hold;
-                        if (!h) {
-                            const int tok = ds_token(a);
-                            h = a.embed + (size_t)(tok < 0 ? 0 : tok) * a.H;
-                        }
-                        ea.x = n0 >= 0 ? __ldcg(h + n0) : 0.f;
-                        ea.y = n1 >= 0 ? __ldcg(h + n1) : 0.f;
-                    } else if (ph.emode == DE_QKV && g < d.rope_heads * (HD / 8) && pos < a.max_pos) {
-                        const float *cr = a.rope_cos + (size_t)pos * HD, *sr = a.rope_sin + (size_t)pos * HD;
-                        if (n0 >= 0) {
-                            ea.x = __ldg(cr + n0 % HD);
-                            eb.x = __ldg(sr + n0 % HD);
-                        }
-                        if (n1 >= 0) {
-                            ea.y = __ldg(cr + n1 % HD);
-                            eb.y = __ldg(sr + n1 % HD);
-                        }
-                    }
-                }
                 float2 acc = make_float2(0.f, 0.f);
                 for (int b = 0; b < np; b++) {
                     const int seq = seq_base + r * DS_NCW * np + b * nr + (j - DS_NCW * r);
@@ -586,6 +657,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status) ||
                                  !mbar_wait(&full[s], (seq / S) & 1, a.status))) {
                         bad = true;
+                        s_bad = 1;
                         atomicExch(a.abort, 1);
                     }
                     if (!bad) {
@@ -595,7 +667,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         acc = ds_steps_full<VM>(st, lane, xr + 8 * s0, sf - s0, tab, acc);
                         for (int sg = sf; sg < s1; sg++)
                             acc = ds_step_tail<VM>(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
-                                               len - 8 * sg, tab, acc);
+                                                   len - 8 * sg, tab, acc);
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
@@ -626,7 +698,6 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     if (t == 0 && !bad && pos < a.max_pos) {
                         const bool rot = g < d.rope_heads * (HD / 8);
                         const float yy[2] = {y.x, y.y}, pp[2] = {pr.x, pr.y};
-                        const float cc[2] = {ea.x, ea.y}, sn2[2] = {eb.x, eb.y};
                         const int nn[2] = {n0, n1};
 #pragma unroll
                         for (int k = 0; k < 2; k++) {
@@ -635,21 +706,27 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                             if (rot) {
                                 const int head = n / HD, dim = n % HD;
                                 const float rt = cp < 2 ? -pp[k] : pp[k];
-                                const float v = __fadd_rn(__fmul_rn(yy[k], cc[k]), __fmul_rn(rt, sn2[k]));
-                                if (head < a.nh)
-                                    ds_put(a, DSP_Q, n, v);
-                                else
-                                    ds_put(a, DSP_KC, (((size_t)ph.layer * a.nkv + (head - a.nh)) * a.max_pos + pos) * HD + dim, v);
+                                const float v = __fadd_rn(__fmul_rn(yy[k], rcs[0][dim]),
+                                                          __fmul_rn(rt, rcs[1][dim]));
+                                if (head < a.nh) {
+                                    ds_put_ll(a, DSP_Q, n, v, otag);
+                                } else {
+                                    const int kh = head - a.nh;
+                                    ds_put(a, DSP_KC, (((size_t)ph.layer * a.nkv + kh) * a.max_pos + pos) * HD + dim, v);
+                                    ds_put_ll(a, DSP_KN, kh * HD + dim, v, otag);
+                                }
                             } else {
                                 const int vi = n - a.qd - a.kvd;
                                 ds_put(a, DSP_VC, (((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD, yy[k]);
+                                ds_put_ll(a, DSP_VN, vi, yy[k], otag);
                             }
                         }
                     }
                 } else if (ph.emode == DE_RESID) {
+                    // the residual: the raw x this CTA staged for QKV / gate_up
                     if (t == 0 && !bad) {
-                        if (n0 >= 0) ds_put(a, ph.out_kind, n0, __fadd_rn(ea.x, y.x));
-                        if (n1 >= 0) ds_put(a, ph.out_kind, n1, __fadd_rn(ea.y, y.y));
+                        if (n0 >= 0) ds_put_ll(a, ph.out_kind, n0, __fadd_rn(hsave[n0], y.x), otag);
+                        if (n1 >= 0) ds_put_ll(a, ph.out_kind, n1, __fadd_rn(hsave[n1], y.y), otag);
                     }
                 } else if (ph.emode == DE_SWIGLU) {
                     float2 up;
@@ -662,7 +739,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         for (int k = 0; k < 2; k++) {
                             if (nn[k] < 0) continue;
                             const double dg = (double)yy[k];
-                            ds_put(a, ph.out_kind, nn[k], __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]));
+                            ds_put_ll(a, ph.out_kind, nn[k],
+                                      __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]), otag);
                         }
                     }
                 } else {   // DE_LM
@@ -687,7 +765,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             cbar_sync();   // every warp's outputs are stored and the table is free
             if (tid == 0) mbar_arrive(&tfree[slot]);
             q++;
-            if (ph.emode == DE_LM) {   // this CTA's first maximum
+            if (ph.emode != DE_LM) continue;
+            // ------------------------------------------------ token pick
+            {   // this CTA's first maximum
                 float bv = lm_v;
                 int bi = lm_i;
                 for (int o = 16; o; o >>= 1) {
@@ -719,31 +799,22 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
             }
             if (tid == 0) {
-                // arrive at every rank's counter of this phase
+                // arrive at every rank's lm_head counter
                 int ncta = 0;
                 for (int r = 0; r < a.world; r++) ncta += ds_ncta(a, ph.groups_all, r, G);
-                int prev = 0;
+                bool pick;
                 if (a.world == 1) {
                     __threadfence();
-                    prev = atomicAdd(a.done + p, 1);
+                    pick = atomicAdd(a.done + p, 1) == ncta * ep1 - 1;
                 } else {
                     __threadfence_system();
-                    for (int r = 0; r < a.world; r++) {
-                        const int o = atomicAdd_system(ds_peer<int>(a, DSP_DONE, r) + p, 1);
-                        if (r == a.rank) prev = o;
-                    }
-                }
-                // the token pick runs on every rank: by the last CTA of
-                // this rank to arrive, once every rank's candidates are in
-                bool pick = false;
-                if (ph.emode == DE_LM) {
-                    if (a.world == 1) {
-                        pick = prev == ncta * ep1 - 1;
-                    } else {
-                        const int pl = atomicAdd(a.lm_local, 1);
-                        pick = pl == ds_ncta(a, ph.groups_all, a.rank, G) * ep1 - 1 &&
-                               ds_wait_counter(a.done + p, ncta * ep1, a.status, a.abort);
-                    }
+                    for (int r = 0; r < a.world; r++)
+                        atomicAdd_system(ds_peer<int>(a, DSP_DONE, r) + p, 1);
+                    // the token pick runs on every rank: by the last CTA of
+                    // this rank to arrive, once every rank's candidates are in
+                    const int pl = atomicAdd(a.lm_local, 1);
+                    pick = pl == ds_ncta(a, ph.groups_all, a.rank, G) * ep1 - 1 &&
+                           ds_wait_counter(a.done + p, ncta * ep1, a.status, a.abort);
                 }
                 if (pick) {
                     // the reference's greedy pick: best = logits[0], then
@@ -781,22 +852,34 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             const int l = ph.layer;
             const float *kcl = a.kc + (size_t)l * a.nkv * a.max_pos * HD;
             const float *vcl = a.vc + (size_t)l * a.nkv * a.max_pos * HD;
-            const int pos = a.st->pos;
+            const ll_t *knl = ds_peer<ll_t>(a, DSP_KN, a.rank);
+            const ll_t *vnl = ds_peer<ll_t>(a, DSP_VN, a.rank);
             for (int hq = cta; hq < ph.ntasks; hq += G) {
                 const int g = hq / a.groups;
                 if (pos < a.max_pos) {
-                    for (int d = tid; d < HD; d += DS_NC) qv[d] = __ldcg(a.q + hq * HD + d);
+                    // q of this head and this position's k and v of its
+                    // group (positions before it come from the cache)
+                    for (int i = tid; i < 3 * HD && !bad; i += DS_NC) {
+                        const int part = i / HD, dd = i % HD;
+                        const ll_t *src = part == 0 ? a.q + hq * HD + dd
+                                        : (part == 1 ? knl : vnl) + g * HD + dd;
+                        float *dst = part == 0 ? qv + dd : knv[part - 1] + dd;
+                        if (!ll_fetch1(src, otag, dst, a)) bad = true;
+                    }
+                    if (bad) s_bad = 1;
                     cbar_sync();
+                    if (s_bad) break;
                     const float4 *q4 = reinterpret_cast<const float4 *>(qv);
                     for (int jj = tid; jj <= pos; jj += DS_NC) {
-                        const float4 *kg4 =
-                            reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD);
+                        const float4 *kg4 = jj < pos
+                            ? reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD)
+                            : reinterpret_cast<const float4 *>(knv[0]);
                         float dot = 0.f;
 #pragma unroll
                         for (int e0 = 0; e0 < NQ; e0 += 8) {
                             float4 kk[8];
 #pragma unroll
-                            for (int e = 0; e < 8; e++) kk[e] = __ldcg(kg4 + e0 + e);
+                            for (int e = 0; e < 8; e++) kk[e] = kg4[e0 + e];
 #pragma unroll
                             for (int e = 0; e < 8; e++) {
                                 const float4 qq = q4[e0 + e];
@@ -829,12 +912,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         const int dq = tid % NQ, pg = tid / NQ;
                         const float4 *vg4 =
                             reinterpret_cast<const float4 *>(vcl + (size_t)g * a.max_pos * HD) + dq;
+                        const float4 vnew = reinterpret_cast<const float4 *>(knv[1])[dq];
+                        auto vrow = [&](int j) {
+                            return j < pos ? __ldcg(vg4 + (size_t)j * NQ) : vnew;
+                        };
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         int jj = pg;
                         for (; jj + 3 * NPG <= pos; jj += 4 * NPG) {
                             float4 vj[4];
 #pragma unroll
-                            for (int e = 0; e < 4; e++) vj[e] = __ldcg(vg4 + (size_t)(jj + e * NPG) * NQ);
+                            for (int e = 0; e < 4; e++) vj[e] = vrow(jj + e * NPG);
 #pragma unroll
                             for (int e = 0; e < 4; e++) {
                                 const float pj = sc[jj + e * NPG];
@@ -845,7 +932,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                             }
                         }
                         for (; jj <= pos; jj += NPG) {
-                            const float4 vj = __ldcg(vg4 + (size_t)jj * NQ);
+                            const float4 vj = vrow(jj);
                             const float pj = sc[jj];
                             acc.x = __fadd_rn(acc.x, __fmul_rn(pj, vj.x));
                             acc.y = __fadd_rn(acc.y, __fmul_rn(pj, vj.y));
@@ -858,15 +945,12 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     for (int d = tid; d < HD; d += DS_NC) {
                         float acc = pctx[0][d];
                         for (int i2 = 1; i2 < NPG; i2++) acc = __fadd_rn(acc, pctx[i2][d]);
-                        a.ctx[hq * HD + d] = acc;
+                        st_ll(a.ctx + hq * HD + d, acc, otag);
                     }
                 }
-                cbar_sync();
-                if (tid == 0) {
-                    __threadfence();
-                    atomicAdd(a.done + p, 1);
-                }
+                cbar_sync();   // qv, knv, sc and pctx are free again
             }
+            if (s_bad) break;
         }
     }
 }

@@ -497,6 +497,7 @@ struct DecodePlan {
     size_t cnt_n = 0;
     int *d_abort = nullptr;
     std::vector<void *> ds_bufs;   // device layouts, partials, activations
+    std::vector<std::pair<void *, size_t>> ll_bufs;   // tagged activations (zeroed on reset)
     // column shard: every rank's copy of the shared buffers ([kind][rank])
     int rank = 0, world = 1;
     bool connected = false;
@@ -656,11 +657,11 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     }
     if (!KLLM_CUDA(cudaStreamSynchronize(c->stream))) return false;
     // shared memory: ring | 2 tables | 2 norm weight vectors | staged x
-    // (attention scores alias it) | mbarriers
+    // (attention scores alias it) | saved raw x | mbarriers
     if (H % 4) return false;   // norm weights arrive by bulk copy
     xc_cap = (xc_cap + 3) & ~3;
     const int wn_cap = (H + 3) & ~3;
-    const size_t fixed = (size_t)4 * (2 * tab_cap + 2 * wn_cap + xc_cap) + 8 * 5 + 16;
+    const size_t fixed = (size_t)4 * (2 * tab_cap + 3 * wn_cap + xc_cap) + 8 * 5 + 16;
     if (avail <= fixed + 2 * ((size_t)DS_STAGE + 16)) return false;
     const int S = (int)std::min<size_t>(DS_MAX_STAGES, (avail - fixed) / (DS_STAGE + 20));
     const size_t smem = (size_t)S * DS_STAGE + fixed + (size_t)8 * (2 * S) + (size_t)4 * S;
@@ -679,28 +680,40 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         own(b);
         return b;
     };
-    float *qb = fbuf(qd), *act = fbuf(t.F), *hA = fbuf(H), *hB = fbuf(H);
-    if (!qb || !act || !hA || !hB) return false;
+    // tagged activations (one allocation each: each is a peer buffer);
+    // zero tags never match a step's (ds_tag >= 256)
+    auto llbuf = [&](size_t n) -> ll_t * {
+        ll_t *b = nullptr;
+        const size_t bytes = std::max<size_t>(n, 1) * sizeof(ll_t);
+        if (!KLLM_CUDA(cudaMalloc((void **)&b, bytes)) || !KLLM_CUDA(cudaMemset(b, 0, bytes)))
+            return nullptr;
+        own(b);
+        p->ll_bufs.push_back({b, bytes});
+        return b;
+    };
+    ll_t *qb = llbuf(qd), *act = llbuf(t.F), *hA = llbuf(H), *hB = llbuf(H);
+    ll_t *kn = llbuf(kvd), *vn = llbuf(kvd), *ctxl = llbuf(qd);
+    if (!qb || !act || !hA || !hB || !kn || !vn || !ctxl) return false;
+    if (L > 255) return false;   // ds_tag keeps the layer in 8 bits
     if ((size_t)sms * world > 4096) return false;   // lm_head candidates, one per CTA and rank
     // phases
     std::vector<DSPhase> ph;
-    // CTAs of all ranks with work in a matrix's phase (each arrives once)
-    auto ncta = [&](int mi) {
-        int n = 0;
-        for (int r = 0; r < world; r++) {
-            const int local = r < groups_all[mi] ? (groups_all[mi] - r + world - 1) / world : 0;
-            n += std::min(sms, local);
-        }
-        return n;
+    // The residual epilogues of O and down read the raw x that the same CTA
+    // staged for QKV and gate_up: every CTA with O (down) work must have
+    // QKV (gate_up) work.
+    auto local_groups = [&](int mi) {
+        return rank < groups_all[mi] ? (groups_all[mi] - rank + world - 1) / world : 0;
     };
-    auto gemv = [&](int mi, int xmode, const float *x, const float *nw, float eps, int emode,
-                    const float *hold, float *out, int out_kind, int dep, int dep_count, int layer) {
+    for (int l = 0; l < L; l++)
+        if (std::min(sms, local_groups(4 * l + 1)) > std::min(sms, local_groups(4 * l)) ||
+            std::min(sms, local_groups(4 * l + 3)) > std::min(sms, local_groups(4 * l + 2)))
+            return false;
+    auto gemv = [&](int mi, int xmode, const ll_t *x, const float *nw, float eps, int emode,
+                    int save_x, float *out, int out_kind, int layer, int x_layer) {
         const TTXDesc &d = desc[mi];
         DSPhase m = {};
         m.kind = DS_GEMV;
         m.ntasks = d.ngroups;
-        m.dep = dep;
-        m.dep_count = dep_count;
         m.d = d;
         m.npieces = (d.ns + DS_PIECE_STEPS - 1) / DS_PIECE_STEPS;
         m.xs = xsz[mi];
@@ -713,7 +726,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         m.x = x;
         m.norm_w = nw;
         m.eps = eps;
-        m.hold = hold;
+        m.x_layer = x_layer;
+        m.save_x = save_x;
         m.out = out;
         m.out_kind = out_kind;
         m.groups_all = groups_all[mi];
@@ -721,31 +735,25 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         ph.push_back(m);
         return (int)ph.size() - 1;
     };
-    int prev_dn = -1;
+    // Each phase reads its input words with the tag of the layer that wrote
+    // them: QKV of layer l the residual of down l-1 (layer 0: the embedding
+    // row), attention and the rest of layer l the outputs of layer l.
     for (int l = 0; l < L; l++) {
         const int mq = 4 * l;
-        const int p_qkv =
-            l == 0 ? gemv(mq, DX_EMBED, nullptr, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr,
-                          qb, DSP_Q, -1, 0, l)
-                   : gemv(mq, DX_NORM, hA, p->dev_norm[2 * l], p->eps[2 * l], DE_QKV, nullptr, qb,
-                          DSP_Q, prev_dn, ncta(mq - 1), l);
+        gemv(mq, l == 0 ? DX_EMBED : DX_NORM, l == 0 ? nullptr : hA, p->dev_norm[2 * l],
+             p->eps[2 * l], DE_QKV, 1, nullptr, DSP_Q, l, l - 1);
         DSPhase at = {};
         at.kind = DS_ATT;
         at.ntasks = t.nh;
-        at.dep = p_qkv;
-        at.dep_count = ncta(mq);
         at.layer = l;
         ph.push_back(at);
-        const int p_att = (int)ph.size() - 1;
-        const int p_o = gemv(mq + 1, DX_VEC, p->ctx, nullptr, 0.f, DE_RESID, l == 0 ? nullptr : hA,
-                             hB, DSP_HB, p_att, t.nh, l);
-        const int p_gu = gemv(mq + 2, DX_NORM, hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1],
-                              DE_SWIGLU, nullptr, act, DSP_ACT, p_o, ncta(mq + 1), l);
-        prev_dn = gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, hB, hA, DSP_HA, p_gu,
-                       ncta(mq + 2), l);
+        gemv(mq + 1, DX_VEC, ctxl, nullptr, 0.f, DE_RESID, 0, nullptr, DSP_HB, l, l);
+        gemv(mq + 2, DX_NORM, hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], DE_SWIGLU, 1, nullptr,
+             DSP_ACT, l, l);
+        gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, 0, nullptr, DSP_HA, l, l);
     }
-    gemv(nmat - 1, DX_NORM, hA, p->dev_norm.back(), p->f_eps, DE_LM, nullptr, p->logits, DSP_LOGITS,
-         prev_dn, ncta(nmat - 2), L);
+    gemv(nmat - 1, DX_NORM, hA, p->dev_norm.back(), p->f_eps, DE_LM, 0, p->logits, DSP_LOGITS, L,
+         L - 1);
     const size_t nph = ph.size();
     p->cnt_n = nph + 2;   // done[phases], epoch, this rank's lm_head arrivals
     if (!KLLM_CUDA(cudaMalloc((void **)&p->d_cnt, p->cnt_n * sizeof(int))) ||
@@ -763,7 +771,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     p->peer_host.assign((size_t)DSP_KINDS * world, nullptr);
     {
         void *mine[DSP_KINDS] = {qb, p->kc, p->vc, hA, hB, act, p->logits, p->cand_v, p->cand_i,
-                                 p->d_cnt};
+                                 kn, vn, p->d_cnt};
         for (int k = 0; k < DSP_KINDS; k++) p->peer_host[(size_t)k * world + rank] = mine[k];
     }
     if (!KLLM_CUDA(cudaMalloc((void **)&p->d_peers, p->peer_host.size() * sizeof(void *))) ||
@@ -803,7 +811,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.kc = p->kc;
     a.vc = p->vc;
     a.scale = p->scale;
-    a.ctx = p->ctx;
+    a.ctx = ctxl;
     a.cand_v = p->cand_v;
     a.cand_i = p->cand_i;
     a.rank = rank;
@@ -1277,8 +1285,11 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
     int status = 0;
     if (!KLLM_CUDA(cudaMemcpy(&status, p->status, 4, cudaMemcpyDeviceToHost))) return false;
     if (status) {
-        // an aborted step leaves the arrival counters mid-step: start over
+        // an aborted step leaves the counters mid-step and tagged words of
+        // step numbers that will be reused: start over
         if (p->d_cnt) cudaMemset(p->d_cnt, 0, p->cnt_n * sizeof(int));
+        if (p->d_abort) cudaMemset(p->d_abort, 0, sizeof(int));
+        for (auto &b : p->ll_bufs) cudaMemset(b.first, 0, b.second);
         set_error("decode kernels reported status 0x%x (%s)", status,
                   (status & ST_WAIT_TIMEOUT) ? "a wait timed out" : "a token was out of range");
         return false;
