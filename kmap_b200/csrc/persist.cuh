@@ -82,7 +82,9 @@ struct DSPhase {
     int out_kind;              // DSPeer of the output
     int groups_all;            // column groups of the matrix over all ranks
     int layer;
+    int pad_[3];               // 16-byte multiple: copied into shared memory in 16-byte pieces
 };
+static_assert(sizeof(DSPhase) % 16 == 0, "DSPhase is copied in 16-byte pieces");
 
 struct DSArgs {
     const DSPhase *phases;
@@ -118,9 +120,14 @@ struct DSArgs {
     void *const *peers;
 };
 
+constexpr int DS_MAX_WORLD = 8;
+// DSArgs::peers, copied into shared memory when a step starts: every
+// epilogue store goes through it.
+__shared__ void *ds_speers[DSP_KINDS * DS_MAX_WORLD];
+
 template <class T>
 __device__ __forceinline__ T *ds_peer(const DSArgs &a, int kind, int r) {
-    return reinterpret_cast<T *>(a.peers[kind * a.world + r]);
+    return reinterpret_cast<T *>(ds_speers[kind * a.world + r]);
 }
 
 // Store v at index i of every rank's copy of buffer `kind`.
@@ -379,15 +386,62 @@ __device__ __forceinline__ float2 ds_mac_step(const float *xr, const DSVals &v, 
     return acc;
 }
 
+// One step of a value stream as loaded: the lane's two stream words and
+// its 8 x values.
+struct DSRaw {
+    uint4 q0, q1;
+    float4 xa, xb;
+};
+
+__device__ __forceinline__ DSRaw ds_load_raw(const uint8_t *lp, const float *xr) {
+    DSRaw r;
+    r.q0 = *reinterpret_cast<const uint4 *>(lp);
+    r.q1 = *reinterpret_cast<const uint4 *>(lp + 512);
+    r.xa = *reinterpret_cast<const float4 *>(xr);
+    r.xb = *reinterpret_cast<const float4 *>(xr + 4);
+    return r;
+}
+
+template <int VM>
+__device__ __forceinline__ float2 ds_mac_raw(const DSRaw &r, float2 acc) {
+    const DSVals v = ds_step_vals<VM>(nullptr, r.q0, r.q1);
+    const float xv[8] = {r.xa.x, r.xa.y, r.xa.z, r.xa.w, r.xb.x, r.xb.y, r.xb.z, r.xb.w};
+    float2 pr[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) pr[e] = __fmul2_rn(make_float2(xv[e], xv[e]), v.v[e]);
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc = __fadd2_rn(acc, pr[e]);
+    return acc;
+}
+
 // Steps [0, n) of a piece whose every row is inside the lane's chunk, in
-// order.  Two register sets of two steps each: the codebook values of the
-// next two steps are in flight while the current two are multiplied and
-// added in row order.
+// order.  Two register sets of two steps each: the next two steps' weights
+// (and, for value streams, x) are in flight while the current two are
+// multiplied and added in row order.
 template <int VM>
 __device__ __forceinline__ float2 ds_steps_full(const uint8_t *pc, int lane, const float *xr,
                                                 int n, const float *tab, float2 acc) {
     const uint8_t *lp = pc + lane * 16;
     int i = 0;
+    if constexpr (VM != TTX_VSLOT) {
+        if (n >= 4) {
+            DSRaw a0 = ds_load_raw(lp, xr), a1 = ds_load_raw(lp + TTX_STEP, xr + 8);
+            for (; i + 4 <= n; i += 4) {
+                const DSRaw b0 = ds_load_raw(lp + (i + 2) * TTX_STEP, xr + 8 * i + 16);
+                const DSRaw b1 = ds_load_raw(lp + (i + 3) * TTX_STEP, xr + 8 * i + 24);
+                acc = ds_mac_raw<VM>(a0, acc);
+                acc = ds_mac_raw<VM>(a1, acc);
+                if (i + 6 <= n) {
+                    a0 = ds_load_raw(lp + (i + 4) * TTX_STEP, xr + 8 * i + 32);
+                    a1 = ds_load_raw(lp + (i + 5) * TTX_STEP, xr + 8 * i + 40);
+                }
+                acc = ds_mac_raw<VM>(b0, acc);
+                acc = ds_mac_raw<VM>(b1, acc);
+            }
+        }
+        for (; i < n; i++) acc = ds_mac_raw<VM>(ds_load_raw(lp + i * TTX_STEP, xr + 8 * i), acc);
+        return acc;
+    }
     if (n >= 4) {
         DSVals a0 = ds_load_step<VM>(lp, tab), a1 = ds_load_step<VM>(lp + TTX_STEP, tab);
         for (; i + 4 <= n; i += 4) {
@@ -422,6 +476,28 @@ __device__ __forceinline__ float2 ds_step_tail(const uint8_t *stp, int lane, con
     return acc;
 }
 
+// ttx_col with the head dim a compile-time constant (no divisions).
+template <int HD>
+__device__ __forceinline__ int ds_col(const TTXDesc &d, int g, int c) {
+    if (d.colmode == TTX_GATE_UP) {
+        const int n = 4 * g + (c & 3);
+        if (n >= d.F) return -1;
+        return c < 4 ? n : d.F + n;
+    }
+    if (d.colmode == TTX_ROPE) {
+        constexpr int PH = HD / 8;   // groups per rotated head
+        const int rg = d.rope_heads * PH;
+        if (g < rg) {
+            const int head = g / PH, d0 = (g % PH) * 4;
+            return head * HD + (c < 4 ? d0 + c : d0 + HD / 2 + (c - 4));
+        }
+        const int n = rg * 8 + (g - rg) * 8 + c;
+        return n < d.N ? n : -1;
+    }
+    const int n = g * TTX_GCOLS + c;
+    return n < d.N ? n : -1;
+}
+
 // HD: head dim; VM: what the streams hold (TTXVals, the same for every
 // matrix of the step).
 template <int HD, int VM>
@@ -435,6 +511,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     __shared__ __align__(16) float pctx[NPG][HD];
     __shared__ float rcs[2][HD];               // RoPE cos / sin of this position
     __shared__ int s_bad;                      // a consumer warp gave up a wait
+    __shared__ __align__(16) DSPhase s_ph[2];  // consumers: this phase's and the next one's
     __shared__ int ri[DS_NCW];
     __shared__ float2 sub_y[DS_NCW][4];        // split groups: each warp's column sums
 
@@ -471,6 +548,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         mbar_fence_init();
         s_bad = 0;
     }
+    for (int i = threadIdx.x; i < DSP_KINDS * a.world; i += blockDim.x) ds_speers[i] = a.peers[i];
     __syncthreads();
 
     // ================================================================ producer
@@ -558,13 +636,40 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             rcs[0][d] = __ldg(a.rope_cos + (size_t)pos * HD + d);
             rcs[1][d] = __ldg(a.rope_sin + (size_t)pos * HD + d);
         }
+    // The phase descriptors come through shared memory: warp 0 copies the
+    // next one while the current phase runs (cp.async, waited for before
+    // the phase's closing barrier).
+    auto ph_fetch = [&](int p) {
+        if (warp == 0 && p < a.nphases) {
+            const char *src = reinterpret_cast<const char *>(a.phases + p);
+            char *dst = reinterpret_cast<char *>(&s_ph[p & 1]);
+            for (int i = lane; i < (int)sizeof(DSPhase) / 16; i += 32) cp_async16(dst + 16 * i, src + 16 * i);
+            cp_async_commit();
+        }
+    };
+    auto ph_ready = [&]() {
+        if (warp == 0) cp_async_wait_all();
+    };
+    ph_fetch(0);
+    ph_ready();
+    cbar_sync();
     int seq_base = 0, q = 0;
     float lm_v = -INFINITY;                    // this warp's first maximum
     int lm_i = -1;
     bool bad = false;                          // this warp gave up a wait
     for (int p = 0; p < a.nphases; p++) {
-        const DSPhase &ph = a.phases[p];
-        if (cta >= ph.ntasks) continue;
+        // Warp 0 refills the other slot while this phase runs, so that slot
+        // (the previous phase's) is not read from here on, and this one is
+        // not read after the phase's closing barrier except by the last
+        // phase (lm_head: nothing is fetched after it).
+        const DSPhase &ph = s_ph[p & 1];
+        const int ntasks = ph.ntasks, emode = ph.emode;
+        ph_fetch(p + 1);
+        if (cta >= ntasks) {
+            ph_ready();
+            cbar_sync();
+            continue;
+        }
         const uint32_t otag = ds_tag(ep1, ph.layer);
         if (ph.kind == DS_GEMV) {
             const TTXDesc &d = ph.d;
@@ -628,6 +733,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 const float tot = ds_block_sum(ss, red);
                 const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)K), ph.eps);
                 const float rsq = (float)(1.0 / sqrt((double)add));
+#pragma unroll 4
                 for (int r = lane; r < wrows; r += 32) {
                     const int o = slot_of(r);
                     xc[o] = __fmul_rn(__fmul_rn(xc[o], rsq), wn[wk0 + r]);
@@ -636,20 +742,20 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             cbar_sync();
             if (s_bad) break;   // uniform: every consumer warp leaves together
             // ------------------------------------------------ tasks
-            const int W = d.W;
+            const int W = d.W, lw = __ffs(W) - 1;   // W is 1, 2, 4 or 8
             const int J = (ph.ntasks - cta + G - 1) / G * W, ns = d.ns, np = ph.npieces;
             const int nfull = d.base / 8;             // steps inside every chunk
             // warp task j: sub-task w = j % W of group m = j / W; a group's W
             // sub-tasks sit on W adjacent warps of one round
             for (int j = warp; j < J; j += DS_NCW) {
                 const int r = j / DS_NCW, nr = min(DS_NCW, J - DS_NCW * r);
-                const int m = j / W, w = j % W;
+                const int m = j >> lw, w = j & (W - 1);
                 const int g = (cta + m * G) * a.world + a.rank;   // the matrix's group
                 const int ch = DS_NCW * w + t;        // this lane's chunk
                 const int len = d.chunk_len(ch);
                 const float *xr = ch < d.T ? xc + ch * xs : xc;
                 const int nch = min(DS_NCW, d.T - DS_NCW * w);   // chunks in this sub-task
-                const int n0 = ttx_col(d, g, 2 * cp), n1 = ttx_col(d, g, 2 * cp + 1);
+                const int n0 = ds_col<HD>(d, g, 2 * cp), n1 = ds_col<HD>(d, g, 2 * cp + 1);
                 float2 acc = make_float2(0.f, 0.f);
                 for (int b = 0; b < np; b++) {
                     const int seq = seq_base + r * DS_NCW * np + b * nr + (j - DS_NCW * r);
@@ -672,15 +778,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
                 }
-                // chunk sums in chunk order
+                // chunk sums in chunk order (every lane of the pair gets them)
                 float2 y;
                 y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
                 y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
-                for (int tt = 1; tt < nch; tt++) {
+#pragma unroll
+                for (int tt = 1; tt < DS_NCW; tt++) {
                     float2 o;
                     o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
                     o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
-                    y = __fadd2_rn(y, o);
+                    if (tt < nch) y = __fadd2_rn(y, o);
                 }
                 if (W > 1) {   // sub-task sums of the group, in w order
                     const int bar_id = 2 + warp / W;
@@ -691,81 +798,64 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(32 * W) : "memory");
                     if (w != 0) continue;   // the group's first warp stores the result
                 }
+                // Epilogue: lane t = k of each pair stores column k of it.
+                const int ek = t;                     // 0, 1: this lane's column
+                const int n = ek ? n1 : n0;
+                const float yk = ek ? y.y : y.x;
                 if (ph.emode == DE_QKV) {
                     float2 pr;   // rotate-half partner (pair cp ^ 2)
                     pr.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
                     pr.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
-                    if (t == 0 && !bad && pos < a.max_pos) {
-                        const bool rot = g < d.rope_heads * (HD / 8);
-                        const float yy[2] = {y.x, y.y}, pp[2] = {pr.x, pr.y};
-                        const int nn[2] = {n0, n1};
-#pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const int n = nn[k];
-                            if (n < 0) continue;
-                            if (rot) {
-                                const int head = n / HD, dim = n % HD;
-                                const float rt = cp < 2 ? -pp[k] : pp[k];
-                                const float v = __fadd_rn(__fmul_rn(yy[k], rcs[0][dim]),
-                                                          __fmul_rn(rt, rcs[1][dim]));
-                                if (head < a.nh) {
-                                    ds_put_ll(a, DSP_Q, n, v, otag);
-                                } else {
-                                    const int kh = head - a.nh;
-                                    ds_put(a, DSP_KC, (((size_t)ph.layer * a.nkv + kh) * a.max_pos + pos) * HD + dim, v);
-                                    ds_put_ll(a, DSP_KN, kh * HD + dim, v, otag);
-                                }
+                    if (ek < 2 && n >= 0 && !bad && pos < a.max_pos) {
+                        if (g < d.rope_heads * (HD / 8)) {
+                            const int head = n / HD, dim = n % HD;
+                            const float pk = ek ? pr.y : pr.x;
+                            const float rt = cp < 2 ? -pk : pk;
+                            const float v = __fadd_rn(__fmul_rn(yk, rcs[0][dim]),
+                                                      __fmul_rn(rt, rcs[1][dim]));
+                            if (head < a.nh) {
+                                ds_put_ll(a, DSP_Q, n, v, otag);
                             } else {
-                                const int vi = n - a.qd - a.kvd;
-                                ds_put(a, DSP_VC, (((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD, yy[k]);
-                                ds_put_ll(a, DSP_VN, vi, yy[k], otag);
+                                const int kh = head - a.nh;
+                                ds_put(a, DSP_KC, (((size_t)ph.layer * a.nkv + kh) * a.max_pos + pos) * HD + dim, v);
+                                ds_put_ll(a, DSP_KN, kh * HD + dim, v, otag);
                             }
+                        } else {
+                            const int vi = n - a.qd - a.kvd;
+                            ds_put(a, DSP_VC, (((size_t)ph.layer * a.nkv + vi / HD) * a.max_pos + pos) * HD + vi % HD, yk);
+                            ds_put_ll(a, DSP_VN, vi, yk, otag);
                         }
                     }
                 } else if (ph.emode == DE_RESID) {
                     // the residual: the raw x this CTA staged for QKV / gate_up
-                    if (t == 0 && !bad) {
-                        if (n0 >= 0) ds_put_ll(a, ph.out_kind, n0, __fadd_rn(hsave[n0], y.x), otag);
-                        if (n1 >= 0) ds_put_ll(a, ph.out_kind, n1, __fadd_rn(hsave[n1], y.y), otag);
-                    }
+                    if (ek < 2 && n >= 0 && !bad)
+                        ds_put_ll(a, ph.out_kind, n, __fadd_rn(hsave[n], yk), otag);
                 } else if (ph.emode == DE_SWIGLU) {
                     float2 up;
                     up.x = __shfl_xor_sync(0xffffffffu, y.x, 16);
                     up.y = __shfl_xor_sync(0xffffffffu, y.y, 16);
-                    if (t == 0 && cp < 2 && !bad) {
-                        const float yy[2] = {y.x, y.y}, uu[2] = {up.x, up.y};
-                        const int nn[2] = {n0, n1};
-#pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            if (nn[k] < 0) continue;
-                            const double dg = (double)yy[k];
-                            ds_put_ll(a, ph.out_kind, nn[k],
-                                      __fmul_rn((float)(dg / (1.0 + exp(-dg))), uu[k]), otag);
-                        }
+                    if (ek < 2 && cp < 2 && n >= 0 && !bad) {
+                        const double dg = (double)yk;
+                        ds_put_ll(a, ph.out_kind, n,
+                                  __fmul_rn((float)(dg / (1.0 + exp(-dg))), ek ? up.y : up.x), otag);
                     }
                 } else {   // DE_LM
-                    if (t == 0 && !bad) {
-                        const float yy[2] = {y.x, y.y};
-                        const int nn[2] = {n0, n1};
-#pragma unroll
-                        for (int k = 0; k < 2; k++) {
-                            const int n = nn[k];
-                            if (n < 0) continue;
-                            ds_put(a, ph.out_kind, n, yy[k]);
-                            if (a.hist && pos < a.hist_rows) a.hist[(size_t)pos * d.N + n] = yy[k];
-                            if (yy[k] > lm_v || (yy[k] == lm_v && lm_i >= 0 && n < lm_i)) {
-                                lm_v = yy[k];
-                                lm_i = n;
-                            }
+                    if (ek < 2 && n >= 0 && !bad) {
+                        ds_put(a, ph.out_kind, n, yk);
+                        if (a.hist && pos < a.hist_rows) a.hist[(size_t)pos * d.N + n] = yk;
+                        if (yk > lm_v || (yk == lm_v && lm_i >= 0 && n < lm_i)) {
+                            lm_v = yk;
+                            lm_i = n;
                         }
                     }
                 }
             }
             seq_base += J * np;
+            ph_ready();
             cbar_sync();   // every warp's outputs are stored and the table is free
             if (tid == 0) mbar_arrive(&tfree[slot]);
             q++;
-            if (ph.emode != DE_LM) continue;
+            if (emode != DE_LM) continue;
             // ------------------------------------------------ token pick
             {   // this CTA's first maximum
                 float bv = lm_v;
@@ -854,7 +944,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             const float *vcl = a.vc + (size_t)l * a.nkv * a.max_pos * HD;
             const ll_t *knl = ds_peer<ll_t>(a, DSP_KN, a.rank);
             const ll_t *vnl = ds_peer<ll_t>(a, DSP_VN, a.rank);
-            for (int hq = cta; hq < ph.ntasks; hq += G) {
+            for (int hq = cta; hq < ntasks; hq += G) {
                 const int g = hq / a.groups;
                 if (pos < a.max_pos) {
                     // q of this head and this position's k and v of its
@@ -948,11 +1038,13 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         st_ll(a.ctx + hq * HD + d, acc, otag);
                     }
                 }
+                ph_ready();
                 cbar_sync();   // qv, knv, sc and pctx are free again
             }
             if (s_bad) break;
         }
     }
+    ph_ready();   // no copy into shared memory outlives the CTA
 }
 
 }  // namespace kllm
