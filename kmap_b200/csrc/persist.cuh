@@ -959,27 +959,42 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     if (bad) s_bad = 1;
                     cbar_sync();
                     if (s_bad) break;
-                    const float4 *q4 = reinterpret_cast<const float4 *>(qv);
-                    for (int jj = tid; jj <= pos; jj += DS_NC) {
-                        const float4 *kg4 = jj < pos
-                            ? reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD)
-                            : reinterpret_cast<const float4 *>(knv[0]);
-                        float dot = 0.f;
+                    // scores: 8 threads per position (HD / 8 dims each, summed in
+                    // order, then combined by a fixed butterfly), four
+                    // positions per thread in flight
+                    {
+                        constexpr int TPP = 8, DQ = NQ / TPP;   // float4 per thread and row
+                        const int sub = tid % TPP, pl = tid / TPP;   // 32 position lanes
+                        const float4 *q4 = reinterpret_cast<const float4 *>(qv) + sub * DQ;
+                        for (int base = 0; base <= pos; base += 4 * (DS_NC / TPP)) {
+                            float4 kk[4][DQ];
 #pragma unroll
-                        for (int e0 = 0; e0 < NQ; e0 += 8) {
-                            float4 kk[8];
+                            for (int k = 0; k < 4; k++) {
+                                const int jj = min(base + pl + k * (DS_NC / TPP), pos);
+                                const float4 *kg4 = jj < pos
+                                    ? reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD)
+                                    : reinterpret_cast<const float4 *>(knv[0]);
 #pragma unroll
-                            for (int e = 0; e < 8; e++) kk[e] = kg4[e0 + e];
+                                for (int e = 0; e < DQ; e++) kk[k][e] = kg4[sub * DQ + e];
+                            }
 #pragma unroll
-                            for (int e = 0; e < 8; e++) {
-                                const float4 qq = q4[e0 + e];
-                                dot = __fadd_rn(dot, __fmul_rn(qq.x, kk[e].x));
-                                dot = __fadd_rn(dot, __fmul_rn(qq.y, kk[e].y));
-                                dot = __fadd_rn(dot, __fmul_rn(qq.z, kk[e].z));
-                                dot = __fadd_rn(dot, __fmul_rn(qq.w, kk[e].w));
+                            for (int k = 0; k < 4; k++) {
+                                float dot = 0.f;
+#pragma unroll
+                                for (int e = 0; e < DQ; e++) {
+                                    const float4 qq = q4[e];
+                                    dot = __fadd_rn(dot, __fmul_rn(qq.x, kk[k][e].x));
+                                    dot = __fadd_rn(dot, __fmul_rn(qq.y, kk[k][e].y));
+                                    dot = __fadd_rn(dot, __fmul_rn(qq.z, kk[k][e].z));
+                                    dot = __fadd_rn(dot, __fmul_rn(qq.w, kk[k][e].w));
+                                }
+                                dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, 1));
+                                dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, 2));
+                                dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, 4));
+                                const int jj = base + pl + k * (DS_NC / TPP);
+                                if (sub == 0 && jj <= pos) sc[jj] = __fmul_rn(dot, a.scale);
                             }
                         }
-                        sc[jj] = __fmul_rn(dot, a.scale);
                     }
                     cbar_sync();
                     float m = -INFINITY;
@@ -1008,12 +1023,12 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         };
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         int jj = pg;
-                        for (; jj + 3 * NPG <= pos; jj += 4 * NPG) {
-                            float4 vj[4];
+                        for (; jj + 7 * NPG <= pos; jj += 8 * NPG) {
+                            float4 vj[8];
 #pragma unroll
-                            for (int e = 0; e < 4; e++) vj[e] = vrow(jj + e * NPG);
+                            for (int e = 0; e < 8; e++) vj[e] = vrow(jj + e * NPG);
 #pragma unroll
-                            for (int e = 0; e < 4; e++) {
+                            for (int e = 0; e < 8; e++) {
                                 const float pj = sc[jj + e * NPG];
                                 acc.x = __fadd_rn(acc.x, __fmul_rn(pj, vj[e].x));
                                 acc.y = __fadd_rn(acc.y, __fmul_rn(pj, vj[e].y));
