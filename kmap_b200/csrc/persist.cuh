@@ -220,7 +220,6 @@ __device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *sta
             atomicOr(status, ST_WAIT_TIMEOUT);
             return false;
         }
-        __nanosleep(32);
     }
     return true;
 }
@@ -255,7 +254,6 @@ __device__ __forceinline__ bool ll_fetch(const ll_t *src, int n, uint32_t tag,
         for (int u = 0; u < LL_BATCH; u++)
             if ((uint32_t)(w[u] >> 32) == tag) pend &= ~(1u << u);
         if (!pend) break;
-        __nanosleep(32);
 #pragma unroll
         for (int u = 0; u < LL_BATCH; u++)
             if (pend >> u & 1u) w[u] = ld_ll(src + 32 * u);
