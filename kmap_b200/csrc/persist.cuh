@@ -15,11 +15,11 @@
 // warp: bulk-copies each phase's codebook table (slot streams only) and
 // norm weights into one of two slots, two phases ahead.
 //
-// Consumers, per phase: wait until every CTA finished the phase this one
-// reads (a device-wide counter, polled with a time limit); stage x in
-// shared memory, chunk by chunk (rmsnorm of the residual, the embedding row
-// in layer 0, or a plain vector: ctx, act).  GEMV task, lane = 8 * pair +
-// chunk, two columns per lane:
+// Consumers, per phase: stage x in shared memory, chunk by chunk, by
+// polling the tagged words the producing phase stores (waiting for the
+// input and reading it are one poll, bounded in time); then rmsnorm of the
+// residual, the embedding row in layer 0, or a plain vector (ctx, act).
+// GEMV task, lane = 8 * pair + chunk, two columns per lane:
 //   rows   acc = fl(acc + fl(x[k] * w[k][n])) over the chunk's rows in
 //          order -- the reference's serial chunk sum (_tape_runner.c:530-545);
 //          w[k][n] is codebook[idx[k][n]], read from the stream's value
@@ -28,9 +28,11 @@
 //          (_tape_runner.c:646-662): every TT-GEMV result is bit-identical
 //          to the reference's (fast order: W partial sums in w order);
 //   out    RoPE + KV append (QKV), residual add (O, down), silu(gate) * up
-//          (gate_up), logits + first maximum (lm_head; the CTA that finishes
-//          last picks the token).
-// Attention: one head per task; q and the cache are final by then.
+//          (gate_up), logits + first maximum (lm_head; the CTA that arrives
+//          last on the lm_head counter, the step's only counter, picks the
+//          token).
+// Attention: one head per task; q and this position's k, v are polled as
+// tagged words, earlier positions read from the cache.
 //
 // Every wait is bounded; a wait that gives up raises the abort flag, and
 // the consumers of every CTA leave at the next phase boundary together
@@ -89,7 +91,8 @@ static_assert(sizeof(DSPhase) % 16 == 0, "DSPhase is copied in 16-byte pieces");
 struct DSArgs {
     const DSPhase *phases;
     int nphases;
-    int *done;                 // [nphases] arrivals, counting up across steps
+    int *done;                 // [nphases] arrivals, counting up across steps (only the
+                               // lm_head phase's entry is used)
     int *epoch;                // steps completed since the counters were zeroed
     int *lm_local;             // lm_head arrivals of this rank's CTAs only
     int *status;
