@@ -190,6 +190,41 @@ def ttgemv_once(K, N, C, reps):
     log("ttgemv %dx%d ok" % (K, N))
 
 
+def ttgemm_time(rows, K, N, C, reps):
+    """kllm_tt_gemm on one seeded shape (prefill: `rows` prompt positions):
+    mean device time over `reps` launches after one warm-up, as ms, FP32
+    operations per second (one multiply and one add per weight and row) and
+    rows per second."""
+    import torch
+
+    import kmap_b200
+    lib = kmap_b200.lib()
+    x, cb, idx = chipgen.tt_case(9, K, N, C, rows=rows)
+    dev = torch.device("cuda", 0)
+    di = torch.from_numpy(idx.view(np.int16)).to(dev)
+    dc = torch.from_numpy(np.pad(cb, (0, (-len(cb)) % 4))).to(dev)
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.empty((rows, N), device=dev)
+    s = torch.cuda.current_stream()
+    out = {}
+    for name in ("kllm_tt_gemm",):
+        f = getattr(lib, name)
+        call = lambda: f(dx.data_ptr(), rows, dc.data_ptr(), C, di.data_ptr(), K, N,
+                         dy.data_ptr(), s.cuda_stream)
+        assert call() == 0, kmap_b200.last_error()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            call()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        out[name] = {"ms": ms, "tops": 2.0 * rows * K * N / (ms * 1e-3) / 1e12,
+                     "rows_per_s": rows / (ms * 1e-3)}
+    log("tt-gemm %dx%dx%d codes %d: %s" % (rows, K, N, C, json.dumps(out)))
+    return out
+
+
 # ---------------------------------------------------------------- arms ---
 
 def reference_sample(chip, n_prompt=4, n_gen=4, threads=None):
@@ -392,10 +427,16 @@ def main():
                     help="profiling aid: decode on a TinyLlama-width chip with this many "
                          "layers (small enough for a profiler), print ms per tape step, "
                          "exit (no JSON line)")
+    ap.add_argument("--ttgemm-shape", type=int, nargs=4, metavar=("ROWS", "K", "N", "CODES"),
+                    help="profiling aid: time kllm_tt_gemm (prefill TT-GEMM) on one seeded "
+                         "shape over --steps launches, beside kllm_tt_gemv, and exit")
     ap.add_argument("--ttgemv-shape", type=int, nargs=3, metavar=("K", "N", "CODES"),
                     help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
                          "--steps times and exit (no JSON line)")
     args = ap.parse_args()
+    if args.ttgemm_shape:
+        ttgemm_time(*args.ttgemm_shape, reps=args.steps)
+        return
     if args.ttgemv_shape:
         ttgemv_once(*args.ttgemv_shape, reps=args.steps)
         return

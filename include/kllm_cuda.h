@@ -153,6 +153,16 @@ int kllm_tt_gemv(const float *x, int rows, const float *codebook, int n_codes,
 int kllm_tt_gemv_host(const float *x, int rows, const float *codebook,
                       int n_codes, const uint16_t *idx, int K, int N, float *y);
 
+/* TT-GEMM: the same product for many rows at once (prefill: every prompt
+ * position against one MATMUL_TT weight), each row bit-identical to
+ * kllm_tt_gemv of that row (the reference order of _tape_runner.c:474-663 per
+ * row).  x is [rows][K] and y [rows][N], device memory; the decoded weight
+ * tile is reused across 64 rows, so this form is bound by the FP32 pipes
+ * rather than by the index stream.  Allocates nothing.  Every index must be
+ * < n_codes; rows <= 4194240.  Returns 0 or non-zero (kllm_last_error). */
+int kllm_tt_gemm(const float *x, int rows, const float *codebook, int n_codes,
+                 const uint16_t *idx, int K, int N, float *y, void *stream);
+
 /* Allocation-free form of kllm_tt_gemv for one row (x is [K], y is [N]).
  * No counterpart in the reference runtime.  For callers that may not
  * allocate device memory -- code running during CUDA graph capture, plugins

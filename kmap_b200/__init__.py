@@ -40,6 +40,8 @@ _SIGS = {
     "kllm_default_infer_opts": (None, [C.c_void_p]),
     "kllm_tt_gemv": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                 C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "kllm_tt_gemm": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                               C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "kllm_tt_gemv_host": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                      C.c_int, C.c_int, C.c_void_p]),
     "kllm_chip_open": (C.c_void_p, [C.c_char_p]),
