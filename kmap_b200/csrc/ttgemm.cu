@@ -26,7 +26,9 @@ constexpr int GT = 256;   // threads: 16 column groups of 8 x 16 row groups of 4
 __global__ void __launch_bounds__(GT, 2)
 k_tt_gemm(const float *__restrict__ x, int rows, const float *__restrict__ cb,
           const uint16_t *__restrict__ idx, int K, int N, int T, float *__restrict__ y) {
-    __shared__ __align__(16) float xs[2][GK][GM];   // x slice, k-major
+    // x slice, k-major; rows padded to 68 floats so the transposing stores
+    // spread over the banks (float4 reads stay 16-byte aligned)
+    __shared__ __align__(16) float xs[2][GK][GM + 4];
     __shared__ __align__(16) float ws[2][GK][GN];   // decoded weights
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int r0 = blockIdx.y * GM, n0 = blockIdx.x * GN;
@@ -95,8 +97,10 @@ k_tt_gemm(const float *__restrict__ x, int rows, const float *__restrict__ cb,
                     kend += base + (t < rem ? 1 : 0);
                 }
                 const float4 a = *reinterpret_cast<const float4 *>(&xs[b][kk][ty * 4]);
-                const float4 w0 = *reinterpret_cast<const float4 *>(&ws[b][kk][tx * 8]);
-                const float4 w1 = *reinterpret_cast<const float4 *>(&ws[b][kk][tx * 8 + 4]);
+                // columns tx*4 .. +3 and 64 + tx*4 .. +3: 16 lanes read 256
+                // contiguous bytes per half, without bank conflicts
+                const float4 w0 = *reinterpret_cast<const float4 *>(&ws[b][kk][tx * 4]);
+                const float4 w1 = *reinterpret_cast<const float4 *>(&ws[b][kk][GN / 2 + tx * 4]);
                 const float av[4] = {a.x, a.y, a.z, a.w};
                 const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
@@ -116,7 +120,7 @@ k_tt_gemm(const float *__restrict__ x, int rows, const float *__restrict__ cb,
         if (r >= rows) continue;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            const int n = n0 + tx * 8 + j;
+            const int n = n0 + (j < 4 ? tx * 4 + j : GN / 2 + tx * 4 + (j - 4));
             if (n < N) y[(size_t)r * N + n] = out[i][j];
         }
     }
