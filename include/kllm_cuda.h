@@ -72,7 +72,11 @@ typedef struct {
     int logits_rows;         /* capacity of logits_out in rows */
     int use_graphs;          /* replay each step as a CUDA graph (fused) */
     int order;               /* KLLM_ORDER_*, fused decode step */
-    int reserved[7];
+    int prefill;             /* 1: the prompt's positions but the last run as one
+                                batched pass (TT-GEMMs, kllm_tt_gemm) instead of
+                                one tape step each (persistent plan, one GPU, no
+                                logits_out); 0: the default, step by step */
+    int reserved[6];
 } kllm_infer_opts;
 
 typedef struct {

@@ -142,7 +142,8 @@ def require_gpu():
 
 class InferOpts(C.Structure):
     _fields_ = [("mode", C.c_int), ("logits_out", C.c_void_p), ("logits_rows", C.c_int),
-                ("use_graphs", C.c_int), ("order", C.c_int), ("reserved", C.c_int * 7)]
+                ("use_graphs", C.c_int), ("order", C.c_int), ("prefill", C.c_int),
+                ("reserved", C.c_int * 6)]
 
 
 class InferStats(C.Structure):
@@ -192,9 +193,10 @@ INFO_KEYS = ("vocab_size", "hidden_dim", "num_layers", "num_kv_heads", "head_dim
 class Chip:
     """A chip directory loaded into a device tape context."""
 
-    def __init__(self, path: str, order: int = 0):
+    def __init__(self, path: str, order: int = 0, prefill: bool = False):
         self.path = path
         self.order = order        # ORDER_EXACT / ORDER_FAST for the fused decode step
+        self.prefill = prefill    # batched prompt pass (kllm_infer_opts.prefill)
         h = lib().kllm_chip_open(path.encode())
         if not h:
             msg = last_error()
@@ -233,6 +235,7 @@ class Chip:
         o.mode = mode
         o.use_graphs = 1 if use_graphs else 0
         o.order = self.order if order is None else order
+        o.prefill = 1 if self.prefill else 0
         if logits is not None:
             assert logits.dtype == np.float32 and logits.flags.c_contiguous
             o.logits_out = logits.ctypes.data

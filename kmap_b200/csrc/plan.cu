@@ -38,6 +38,7 @@
 #include "sm100.cuh"
 #include "tt_fused.cuh"
 #include "persist.cuh"
+#include "prefill.cuh"
 
 namespace kllm {
 
@@ -673,13 +674,6 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     if (!KLLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DS_THREADS, smem)) ||
         per_sm < 1)
         return false;
-    // activations
-    auto fbuf = [&](size_t n) -> float * {
-        float *b = nullptr;
-        if (!KLLM_CUDA(cudaMalloc((void **)&b, std::max<size_t>(n, 1) * 4))) return nullptr;
-        own(b);
-        return b;
-    };
     // tagged activations (one allocation each: each is a peer buffer);
     // zero tags never match a step's (ds_tag >= 256)
     auto llbuf = [&](size_t n) -> ll_t * {
@@ -1197,6 +1191,77 @@ static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
     return true;
 }
 
+// Batched prompt pass (KLLM infer option `prefill`): positions 0..R-1 of
+// the prompt through every layer at once -- projections as TT-GEMMs (rows
+// bit-identical to the TT-GEMV), norms, RoPE, causal attention, residuals
+// and SwiGLU as row kernels -- leaving the KV cache of those positions as
+// the per-token steps would.  The last layer needs only its k and v.  The
+// prompt's last position then runs as a regular decode step, which picks
+// the first token.  Buffers are allocated for the call and freed after it.
+static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
+    const TemplateInfo &t = p->ti;
+    const TapeCtx *ctx = &c->base;
+    const int H = t.H, hd = t.hd, nh = t.nh, nkv = t.nkv, F = t.F, L = t.L;
+    const int qd = nh * hd, kvd = nkv * hd, nq = qd + 2 * kvd, mp = p->max_pos;
+    if (R <= 0) return true;
+    if ((size_t)(R + 1) * 4 > 200 * 1024) {
+        set_error("prefill: %d positions exceed the attention kernel's score buffer", R);
+        return false;
+    }
+    float *hA = nullptr, *hB = nullptr, *xn = nullptr, *big = nullptr, *qr = nullptr,
+          *cx = nullptr, *act = nullptr;
+    const size_t wide = (size_t)R * std::max({(size_t)nq, (size_t)2 * F, (size_t)H});
+    bool ok = KLLM_CUDA(cudaMallocAsync((void **)&hA, (size_t)R * H * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&hB, (size_t)R * H * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&xn, (size_t)R * H * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&big, wide * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&qr, (size_t)R * qd * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&cx, (size_t)R * qd * 4, s)) &&
+              KLLM_CUDA(cudaMallocAsync((void **)&act, (size_t)R * F * 4, s));
+    auto gemm = [&](int slot, const float *x, float *y) {
+        const Slot &sl = ctx->slots[slot];
+        const DevSlot &w = c->ds[slot];
+        return kllm_tt_gemm(x, R, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
+    };
+    const int ew_blocks = 148 * 8;
+    const size_t att_smem = (size_t)(R + 1) * 4;
+    if (ok && att_smem > 48 * 1024)
+        ok = KLLM_CUDA(cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)att_smem));
+    if (ok) {
+        k_pf_embed<<<R, PF_THREADS, 0, s>>>(p->embed, p->prompt, H, hA);
+        g_launches++;
+    }
+    for (int l = 0; ok && l < L; l++) {
+        const LayerSlots &ls = t.layers[l];
+        float *kc = p->kc + (size_t)l * nkv * mp * hd, *vc = p->vc + (size_t)l * nkv * mp * hd;
+        k_pf_rmsnorm<<<R, PF_THREADS, 0, s>>>(hA, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
+        ok = gemm(ls.qkv, xn, big);
+        if (!ok) break;
+        k_pf_rope_kv<<<R, PF_THREADS, 0, s>>>(big, nq, nh, nkv, hd, p->rcos, p->rsin, mp, qr, kc, vc);
+        g_launches += 2;
+        if (l + 1 == L) break;   // later positions need only this layer's k and v
+        k_pf_attention<<<dim3(R, nh), PF_THREADS, att_smem, s>>>(
+            qr, kc, vc, nh, t.groups, hd, mp, p->scale, cx);
+        ok = gemm(ls.o, cx, big);
+        if (!ok) break;
+        k_pf_add<<<ew_blocks, 256, 0, s>>>(hA, big, (long long)R * H, hB);
+        k_pf_rmsnorm<<<R, PF_THREADS, 0, s>>>(hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], H, xn);
+        ok = gemm(ls.gu, xn, big);
+        if (!ok) break;
+        k_pf_swiglu<<<ew_blocks, 256, 0, s>>>(big, F, (long long)R * F, act);
+        ok = gemm(ls.dn, act, big);
+        if (!ok) break;
+        k_pf_add<<<ew_blocks, 256, 0, s>>>(hB, big, (long long)R * H, hA);
+        g_launches += 5;
+        ok = KLLM_CUDA(cudaGetLastError());
+    }
+    ok = ok && KLLM_CUDA(cudaGetLastError());
+    for (float *b : {hA, hB, xn, big, qr, cx, act})
+        if (b) cudaFreeAsync(b, s);
+    return ok;
+}
+
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,
                 int eos, const std::function<bool(int, int)> &emit, int *generated) {
     DecodePlan *p = c->plan;
@@ -1258,6 +1323,16 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
     };
     if (!KLLM_CUDA(cudaEventRecord(p->ev0, s))) return false;
     int launched = 0;
+    // batched prompt pass for all prompt positions but the last (persistent
+    // single-GPU plan, no per-step logits requested)
+    if (c->opts.prefill && p->persist && p->world == 1 && want_rows == 0 && prompt_len >= 2) {
+        const int R = prompt_len - 1;
+        StepState st1 = {R, prompt_len, 0, 0};
+        if (!plan_prefill(c, p, R, s) ||
+            !KLLM_CUDA(cudaMemcpyAsync(p->st, &st1, sizeof st1, cudaMemcpyHostToDevice, s)))
+            return false;
+        launched = R;
+    }
     for (; launched < prompt_len; launched++)
         if (!launch_step(launched)) return false;
     if (!KLLM_CUDA(cudaEventRecord(p->ev1, s))) return false;
