@@ -225,6 +225,38 @@ def ttgemm_time(rows, K, N, C, reps):
     return out
 
 
+def prefill_run(steps, warmup):
+    """Config-2 workload on the config-0 chip: a 2047-token uniform-random
+    prompt (the chip's 2048 positions less the first generated token), batch
+    1; prompt positions per second of device time, the batched prompt pass
+    (kllm_infer_opts.prefill) beside the step-by-step one.  Prints one JSON
+    line (not part of the default run)."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    path = config0_chip(0)
+    P = 2047
+    prompt = np.random.default_rng(2).integers(3, 32000, P).astype(np.int32)
+    res = {}
+    first = {}
+    for mode in ("batched", "step_by_step"):
+        with kmap_b200.Chip(path, prefill=(mode == "batched")) as chip:
+            ms = []
+            for i in range(warmup + steps):
+                toks = chip.infer(prompt, 1)
+                if i >= warmup:
+                    ms.append(chip.stats()["prefill_ms"])
+            first[mode] = int(toks[0]) if len(toks) else -1
+            res[mode] = {"ms": statistics.median(ms), "tok_s": P / (statistics.median(ms) * 1e-3)}
+    print(json.dumps({"metric": "prefill tok/s (prompt positions per second, device time)",
+                      "value": res["batched"]["tok_s"], "unit": "tok/s", "n_gpus": 1,
+                      "steps": steps, "warmup": warmup, "higher_is_better": True,
+                      "data": "synthetic", "dtype": "f32",
+                      "config": {"workload": "TinyLlama-1.1B-arch TT chip, 2047-token prompt, "
+                                             "batch 1, KV cache filled", "prompt": P},
+                      "batched": res["batched"], "step_by_step": res["step_by_step"],
+                      "first_token_equal": first["batched"] == first["step_by_step"]}))
+
+
 # ---------------------------------------------------------------- arms ---
 
 def reference_sample(chip, n_prompt=4, n_gen=4, threads=None):
@@ -427,6 +459,9 @@ def main():
                     help="profiling aid: decode on a TinyLlama-width chip with this many "
                          "layers (small enough for a profiler), print ms per tape step, "
                          "exit (no JSON line)")
+    ap.add_argument("--prefill", action="store_true",
+                    help="config-2 workload: time a 2047-token prompt, batched prompt pass "
+                         "beside step by step, print one JSON line and exit")
     ap.add_argument("--ttgemm-shape", type=int, nargs=4, metavar=("ROWS", "K", "N", "CODES"),
                     help="profiling aid: time kllm_tt_gemm (prefill TT-GEMM) on one seeded "
                          "shape over --steps launches, beside kllm_tt_gemv, and exit")
@@ -434,6 +469,9 @@ def main():
                     help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
                          "--steps times and exit (no JSON line)")
     args = ap.parse_args()
+    if args.prefill:
+        prefill_run(args.steps, args.warmup)
+        return
     if args.ttgemm_shape:
         ttgemm_time(*args.ttgemm_shape, reps=args.steps)
         return
