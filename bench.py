@@ -15,14 +15,22 @@ Printed JSON line (rank 0):
   value      device time (CUDA events on the executor's stream) of the K calls
   e2e        the same calls timed on the host around the C-ABI call, prompt in
              and tokens out through host buffers
-  roofline   the dominant kernel, the TT-GEMV, timed live on the config-1
-             shapes (K x N in {2048x2048, 2048x5632, 5632x2048, 2048x32000},
-             seeded codebooks, Gaussian-rank indices) over rotating copies
-             larger than L2; bytes = K*N*2 per launch
+  roofline   the decode step kernel (k_decode_step, one launch per tape step):
+             the index stream's bytes / its mean launch time
+  parity     tokens and per-step logits of one call against the compiled
+             reference runtime on the same chip and prompt
   cpu_baseline  the compiled reference runtime (oracle/_ref) on this host,
-             a bounded sample of the same chip (rank 0, N=1)
-For N > 1 every rank decodes its own replica (no data-path collective):
-value = all ranks' tokens / max-over-ranks time, "scaling": "weak".
+             pinned to 8 cores, the full 32 + 128 workload once (rank 0, N=1)
+  prefill    the 2047-token prompt pass on the same chip (N=1)
+  ttgemv_microbench  kllm_tt_gemv (k_tt_fused) on the isolated MATMUL_TT
+             shapes over rotating copies larger than L2
+For N > 1 the N ranks run ONE decode stream column-sharded over the N GPUs
+(every MATMUL_TT's columns split across ranks, NVLink peer stores inside the
+decode kernel): value = that stream's tokens / max-over-ranks time,
+"scaling": "strong"; "replicas" adds N independent single-GPU streams.
+--impl reference: the compiled reference runtime on the host cores, each step
+8 consecutive tape positions of the same 32 + 128 workload (20 steps = one
+whole call).
 """
 from __future__ import annotations
 
@@ -225,54 +233,122 @@ def ttgemm_time(rows, K, N, C, reps):
     return out
 
 
-def prefill_run(steps, warmup):
+REF_CORES = 8   # the reference's TT pool is 8 threads (compile-time fixed)
+
+
+def prefill_measure(path, reps=3):
     """Config-2 workload on the config-0 chip: a 2047-token uniform-random
     prompt (the chip's 2048 positions less the first generated token), batch
-    1; prompt positions per second of device time, the batched prompt pass
-    (kllm_infer_opts.prefill) beside the step-by-step one.  Prints one JSON
-    line (not part of the default run)."""
+    1.  Device time of the prompt pass -- the batched pass (TT-GEMMs and row
+    kernels for positions 0..2045, then position 2046 as a decode step) and
+    the step-by-step one -- and the first token's logits of both (the logits
+    slot after the prompt, max_new = 0)."""
     import kmap_b200
-    kmap_b200.require_gpu()
-    path = config0_chip(0)
     P = 2047
     prompt = np.random.default_rng(2).integers(3, 32000, P).astype(np.int32)
-    res = {}
-    first = {}
+    res, first = {}, {}
     for mode in ("batched", "step_by_step"):
         with kmap_b200.Chip(path, prefill=(mode == "batched")) as chip:
             ms = []
-            for i in range(warmup + steps):
-                toks = chip.infer(prompt, 1)
-                if i >= warmup:
+            for i in range(1 + (reps if mode == "batched" else 1)):
+                chip.infer(prompt, 0)
+                if i >= 1:
                     ms.append(chip.stats()["prefill_ms"])
-            first[mode] = int(toks[0]) if len(toks) else -1
-            res[mode] = {"ms": statistics.median(ms), "tok_s": P / (statistics.median(ms) * 1e-3)}
+            first[mode] = chip.final_logits()
+            m = statistics.median(ms)
+            res[mode] = {"ms": m, "tok_s": P / (m * 1e-3)}
+    a, b = first["batched"], first["step_by_step"]
+    # one multiply and one add per weight and prompt position (the TT-GEMMs)
+    ops = 2.0 * (P - 1) * INDEX_BYTES_PER_TOKEN / 2
+    return {"prompt": P, "value": res["batched"]["tok_s"], "unit": "tok/s",
+            "batched": res["batched"], "step_by_step": res["step_by_step"],
+            "projection_fp32_ops": ops,
+            "fp32_tops_whole_pass": ops / (res["batched"]["ms"] * 1e-3) / 1e12,
+            "first_token": {"equal": int(np.argmax(a)) == int(np.argmax(b)),
+                            "max_abs_logit_diff": float(np.max(np.abs(a - b))),
+                            "allclose_1e-3_1e-4": bool(np.allclose(a, b, rtol=1e-4, atol=1e-3))}}
+
+
+def prefill_run(steps, warmup):
+    """The prefill measurement alone, as one JSON line."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    r = prefill_measure(config0_chip(0), reps=max(steps, 1))
     print(json.dumps({"metric": "prefill tok/s (prompt positions per second, device time)",
-                      "value": res["batched"]["tok_s"], "unit": "tok/s", "n_gpus": 1,
-                      "steps": steps, "warmup": warmup, "higher_is_better": True,
-                      "data": "synthetic", "dtype": "f32",
+                      "value": r["value"], "unit": "tok/s", "n_gpus": 1, "steps": steps,
+                      "warmup": warmup, "higher_is_better": True, "data": "synthetic",
+                      "dtype": "f32",
                       "config": {"workload": "TinyLlama-1.1B-arch TT chip, 2047-token prompt, "
-                                             "batch 1, KV cache filled", "prompt": P},
-                      "batched": res["batched"], "step_by_step": res["step_by_step"],
-                      "first_token_equal": first["batched"] == first["step_by_step"]}))
+                                             "batch 1, KV cache filled", "prompt": r["prompt"]},
+                      "prefill": r}))
 
 
 # ---------------------------------------------------------------- arms ---
 
-def reference_sample(chip, n_prompt=4, n_gen=4, threads=None):
-    """Time the compiled reference runtime on a bounded sample of the chip."""
+def host_cpu():
+    """This host's CPU model and core counts."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": model, "nproc": os.cpu_count(),
+            "affinity": len(os.sched_getaffinity(0))}
+
+
+def pin_reference_cores():
+    """Pin this process to REF_CORES of its allowed cores and size OpenBLAS
+    to them (before the reference library loads), as taskset would."""
+    allowed = sorted(os.sched_getaffinity(0))
+    cores = allowed[:REF_CORES]
+    os.sched_setaffinity(0, cores)
+    os.environ["OPENBLAS_NUM_THREADS"] = str(len(cores))
+    os.environ["OMP_NUM_THREADS"] = str(len(cores))
+    return cores
+
+
+def cpu_sample(out_path):
+    """Child process of the GPU arm: the compiled reference runtime on
+    REF_CORES pinned host cores, the whole config-0 call (32 prompt + 128
+    greedy positions) once, with every position's logits; writes an npz."""
+    cores = pin_reference_cores()
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import harness
+    chip = config0_chip()
+    ref = harness.Ref()
+    h, info = ref.chip(chip)
+    p = prompt_ids()
+    s = ref.session(h, p, GEN)
+    lg = np.zeros((PROMPT + GEN, int(info[0])), np.float32)
+    t = time.perf_counter()
+    n = s.run(PROMPT + GEN, lg)
+    dt = time.perf_counter() - t
+    toks = s.tokens()
+    s.close()
+    ref.L.refh_chip_destroy(h)
+    np.savez(out_path, tokens=toks, logits=lg[:n], seconds=dt, positions=n,
+             cores=len(cores))
+
+
+def reference_baseline(chip_path):
+    """Run cpu_sample in a pinned child process; None without the reference."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import harness
     if not harness.have_ref():
         return None
-    ref = harness.Ref()
-    h, info = ref.chip(chip)
-    p = prompt_ids()[:n_prompt]
-    t = time.perf_counter()
-    toks = ref.infer(h, p, n_gen)
-    dt = time.perf_counter() - t
-    ref.L.refh_chip_destroy(h)
-    return {"value": (n_prompt + len(toks)) / dt, "seconds": dt, "tokens": n_prompt + len(toks)}
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "ref.npz")
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-sample", out],
+                           capture_output=True, text=True)
+        if r.returncode != 0 or not os.path.exists(out):
+            log("reference sample failed: " + r.stderr[-2000:])
+            return None
+        z = np.load(out)
+        return {k: z[k] for k in z.files}
 
 
 def decode_small(layers, steps, warmup):
@@ -293,7 +369,14 @@ def decode_small(layers, steps, warmup):
     chip.close()
 
 
+REF_WINDOW = 8   # tape positions per reference-arm step
+
+
 def run_reference_arm(args, rank, world):
+    """The compiled reference runtime on REF_CORES pinned host cores.  Each
+    step runs the next REF_WINDOW positions of the config-0 call (32 prompt +
+    128 greedy positions, the reference's own greedy loop), so 20 steps time
+    exactly one whole call; a new call starts after position 159."""
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -302,34 +385,66 @@ def run_reference_arm(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable":
                           "the reference runtime was not compiled into oracle/_ref"}))
         return
+    cores = pin_reference_cores()
     chip = config0_chip()
     ref = harness.Ref()
     h, info = ref.chip(chip)
     p = prompt_ids()
-    n_prompt, n_gen = 4, 4   # bounded sample per step: 8 tape steps
+    s = ref.session(h, p, GEN)
     for _ in range(args.warmup):
-        ref.infer(h, p[:n_prompt], n_gen)
-    times = []
+        if s.run(REF_WINDOW) == 0:
+            s.close()
+            s = ref.session(h, p, GEN)
+    s.close()
+    s = ref.session(h, p, GEN)
+    times, tok = [], 0
     for _ in range(args.steps):
         t = time.perf_counter()
-        toks = ref.infer(h, p[:n_prompt], n_gen)
+        n = s.run(REF_WINDOW)
+        if n == 0:   # the call is complete: the next one
+            s.close()
+            s = ref.session(h, p, GEN)
+            n = s.run(REF_WINDOW)
         times.append(time.perf_counter() - t)
+        tok += n
+    s.close()
     ref.L.refh_chip_destroy(h)
-    tok = (n_prompt + len(toks)) * args.steps
     v = tok / sum(times)
-    cores = int(os.environ.get("OPENBLAS_NUM_THREADS", "8"))
+    cpu = host_cpu()
+    sample = ("compiled reference runtime (_tape_runner.c greedy loop), %d TT threads + "
+              "OpenBLAS %d threads pinned to %d of %d cores (%s); each step = the next %d "
+              "tape positions of the 32 + 128 call" % (REF_CORES, len(cores), len(cores),
+                                                     cpu["nproc"], cpu["model"], REF_WINDOW))
     out = {"metric": "decode tok/s (prompt + generated tape steps per second)", "value": v,
            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": 1e3 * sum(times) / args.steps, "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "impl": "reference",
-           "config": {"workload": "TinyLlama-1.1B-arch TT chip, batch-1 greedy decode; "
-                      "bounded sample per step: 4 prompt + 4 generated tokens",
-                      "prompt": n_prompt, "generate": n_gen},
-           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                            "sample": "4 prompt + 4 generated tape steps per step"},
+           "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic", "impl": "reference",
+           "config": {"workload": "TinyLlama-1.1B-arch TT chip (22x2048, 32/4 heads, SwiGLU "
+                      "5632, vocab 32000, bf16-rounded N(0,0.02)), batch-1 greedy decode",
+                      "prompt": PROMPT, "generate": GEN, "tape_steps_per_call": PROMPT + GEN,
+                      "positions_per_step": REF_WINDOW, "positions_timed": tok,
+                      "same_config": True},
+           "host": cpu,
+           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": len(cores),
+                            "kind": "reference", "sample": sample},
            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
+
+
+def time_calls(chip, p, steps, clk_index):
+    """K calls of the workload: device ms, host seconds, launches, tokens."""
+    dev_ms, host_s, launches, tokens = 0.0, 0.0, 0, 0
+    with Clocks(clk_index) as clk:
+        for _ in range(steps):
+            t = time.perf_counter()
+            toks = chip.infer(p, GEN)
+            host_s += time.perf_counter() - t
+            s = chip.stats()
+            dev_ms += s["prefill_ms"] + s["decode_ms"]
+            launches += s["launches"]
+            tokens += PROMPT + len(toks)
+    return dev_ms, host_s, launches, tokens, clk.summary()
 
 
 def run_ours(args, rank, world, local_rank):
@@ -348,7 +463,7 @@ def run_ours(args, rank, world, local_rank):
     chip_path = config0_chip(rank)
     order = kmap_b200.ORDER_FAST if args.order == "fast" else kmap_b200.ORDER_EXACT
     chip = kmap_b200.Chip(chip_path, order=order)
-    shard = args.shard and world > 1
+    shard = world > 1 and not args.replicas
     if shard:   # every rank holds 1/world of the columns; same prompt everywhere
         chip.connect(kmap_b200.exchange_blocks(chip.shard(rank, world)))
         dist.barrier()
@@ -366,23 +481,40 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
 
     barrier()
-    dev_ms, host_s, launches, tokens = 0.0, 0.0, 0, 0
-    with Clocks(local_rank) as clk:
-        for _ in range(args.steps):
-            t = time.perf_counter()
-            toks = chip.infer(p, GEN)
-            host_s += time.perf_counter() - t
-            s = chip.stats()
-            dev_ms += s["prefill_ms"] + s["decode_ms"]
-            launches += s["launches"]
-            tokens += PROMPT + len(toks)
+    dev_ms, host_s, launches, tokens, clocks = time_calls(chip, p, args.steps, local_rank)
     barrier()
     times = torch.tensor([dev_ms, host_s * 1e3], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     dev_ms_max, host_ms_max = times.tolist()
-    if rank != 0:
+    # tokens (and, on one GPU, every step's logits) of one call, for the
+    # parity record (rank 0 compares); a sharded rank holds only its own
+    # columns' logits rows, so N > 1 compares tokens
+    lg_ours = None
+    if world == 1:
+        toks_ours, lg_ours = chip.infer(p, GEN, logits=True)
+    else:
+        toks_ours = chip.infer(p, GEN)
+    replicas = None
+    if shard:
+        # the same workload as N independent single-GPU streams, for context
         chip.close()
+        rchip = kmap_b200.Chip(chip_path, order=order)
+        rp = prompt_ids(seed=rank)
+        for _ in range(max(args.warmup, 1)):
+            rchip.infer(rp, GEN)
+        barrier()
+        r_ms, _, _, r_tok, _ = time_calls(rchip, rp, args.steps, local_rank)
+        barrier()
+        rt = torch.tensor([r_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        replicas = {"value": r_tok * world / (rt.item() / 1e3), "unit": "tok/s",
+                    "streams": world, "scaling": "weak"}
+        rchip.close()
+        chip = None
+    if rank != 0:
+        if chip:
+            chip.close()
         if dist:
             dist.destroy_process_group()
         return
@@ -391,17 +523,12 @@ def run_ours(args, rank, world, local_rank):
     e2e = tokens * streams / (host_ms_max / 1e3)
     pk = peaks()
     hbm = pk.get("hbm_gbs")
-    roof = ttgemv_roofline(local_rank)
-    top = max(roof, key=lambda r: r["K"] * r["N"])
     # the dominant kernel is the decode step (one launch per tape step):
     # its algorithmic bytes are the index stream of every TT matrix
     step_us = dev_ms_max * 1e3 / tokens
     decode_gbs = INDEX_BYTES_PER_TOKEN / (step_us * 1e-6) / 1e9
     # sharded: the index stream is split over the GPUs, so their summed peak
     roof_peak = hbm * world if (shard and hbm) else hbm
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = reference_sample(chip_path)
     out = {
         "metric": "decode tok/s (prompt + generated tape steps per second)",
         "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -412,6 +539,7 @@ def run_ours(args, rank, world, local_rank):
                    "vocab 32000, bf16-rounded N(0,0.02)), batch-1 greedy decode",
                    "prompt": PROMPT, "generate": GEN, "tape_steps_per_call": PROMPT + GEN,
                    "l2": "weights 2.07 GB/token >> 126 MB L2 (no flush needed)",
+                   "order": args.order,
                    "parallelism": ("column-sharded over %d GPUs (NVLink peer stores in the "
                                    "decode kernel)" % world if shard else
                                    "replicas" if world > 1 else "single GPU")},
@@ -424,20 +552,54 @@ def run_ours(args, rank, world, local_rank):
                      "kernel": "k_decode_step", "launch_us": step_us,
                      "algorithmic_bytes_per_launch": INDEX_BYTES_PER_TOKEN,
                      "order": args.order,
-                     "peak_source": ("MEASURED_PEAKS.json hbm_gbs (burst copy)" if hbm
+                     "peak_source": ("MEASURED_PEAKS.json hbm_gbs (burst copy)%s" %
+                                     (" x %d GPUs" % world if shard else "") if hbm
                                      else "fallback 6650 GB/s")},
-        "ttgemv_microbench": {"kernel": "k_ttgemv_tma", "unit": "GB/s", "peak": hbm,
-                              "shape": [top["K"], top["N"]], "achieved": top["gbs"],
-                              "frac": top["gbs"] / hbm if hbm else None, "shapes": roof},
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
-    if cpu:
-        out["cpu_baseline"] = {"value": cpu["value"], "unit": "tok/s", "cores": 8,
-                               "kind": "reference",
-                               "sample": "compiled reference runtime, same chip, 4 prompt + "
-                                         "4 generated tape steps (%.1fs)" % cpu["seconds"]}
+    if replicas:
+        out["replicas"] = replicas
+    if world == 1:
+        roof = ttgemv_roofline(local_rank)
+        for r in roof:
+            r["frac"] = r["gbs"] / hbm if hbm else None
+        top = max(roof, key=lambda r: r["K"] * r["N"])
+        out["ttgemv_microbench"] = {"kernel": "k_tt_fused", "unit": "GB/s", "peak": hbm,
+                                    "shape": [top["K"], top["N"]], "achieved": top["gbs"],
+                                    "frac": top["frac"], "shapes": roof}
+        if not args.no_prefill:
+            try:
+                out["prefill"] = prefill_measure(chip_path)
+            except Exception as e:   # reported, not fatal for the decode line
+                out["prefill"] = {"error": str(e)[:300]}
+    ref = None
+    if not args.no_cpu_baseline and (world == 1 or shard):
+        ref = reference_baseline(chip_path)
+    if ref is not None:
+        n = int(ref["positions"])
+        rt = ref["tokens"]
+        same = len(rt) == len(toks_ours) and bool(np.array_equal(rt, toks_ours))
+        out["parity"] = {"reference": "compiled reference runtime, same chip and prompt",
+                         "tokens_equal": same, "tokens_compared": int(len(rt))}
+        if lg_ours is not None:
+            rows = min(n, PROMPT + GEN - 1)   # the last step's logits pick no token
+            d = np.abs(lg_ours[:rows] - ref["logits"][:rows])
+            out["parity"].update({
+                "max_abs_logit_diff": float(d.max()), "logit_rows": rows,
+                "logits_allclose_1e-3_1e-4": bool(np.allclose(
+                    lg_ours[:rows], ref["logits"][:rows], rtol=1e-4, atol=1e-3))})
+        if world == 1:
+            cpu = host_cpu()
+            v = n / float(ref["seconds"])
+            out["cpu_baseline"] = {
+                "value": v, "unit": "tok/s", "cores": int(ref["cores"]), "kind": "reference",
+                "sample": "compiled reference runtime on %d pinned cores of %d (%s), %d TT "
+                          "threads + OpenBLAS %d: the whole 32 + 128 call once (%d positions, "
+                          "%.1f s)" % (int(ref["cores"]), cpu["nproc"], cpu["model"], REF_CORES,
+                                       int(ref["cores"]), n, float(ref["seconds"]))}
     print(json.dumps(out), flush=True)
-    chip.close()
+    if chip:
+        chip.close()
     if dist:
         dist.destroy_process_group()
 
@@ -449,9 +611,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--shard", action="store_true",
-                    help="with N > 1: one decode stream column-sharded over the N GPUs "
-                         "(strong scaling) instead of N independent replicas")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N > 1: N independent single-GPU decode streams (weak scaling) "
+                         "instead of one stream column-sharded over the N GPUs")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="leave the prefill measurement out of the JSON line")
+    ap.add_argument("--cpu-sample", metavar="OUT", help=argparse.SUPPRESS)
     ap.add_argument("--order", default="exact", choices=["exact", "fast"],
                     help="TT-GEMV summation order of the decode step: the reference's "
                          "chunked order (bit-identical MATMUL_TT) or the finer split")
@@ -469,6 +634,9 @@ def main():
                     help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
                          "--steps times and exit (no JSON line)")
     args = ap.parse_args()
+    if args.cpu_sample:
+        cpu_sample(args.cpu_sample)
+        return
     if args.prefill:
         prefill_run(args.steps, args.warmup)
         return

@@ -5,7 +5,8 @@
 
 Objects go to kmap_b200/_build/, the library to kmap_b200/libkllm_cuda.so.
 The CUDA runtime is linked statically, so the library only needs the NVIDIA
-driver at run time (plus libnccl for multi-GPU contexts).
+driver at run time; the column-sharded decode talks to the other GPUs through
+CUDA IPC mappings inside its own kernel, not through a collectives library.
 """
 from __future__ import annotations
 

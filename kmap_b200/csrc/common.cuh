@@ -122,9 +122,12 @@ bool tt_gemv_partials(cudaStream_t s, const float *x, int rows, const float *cb,
 bool tt_reduce_partials(cudaStream_t s, const float *part, int T, int rows, int N,
                         float *y);
 // One-row TT-GEMV with the ordered reduction fused; false (no error) when
-// the matrix does not meet the TMA rules.
+// the matrix does not meet the TMA rules.  A device wait that gives up sets
+// ST_WAIT_TIMEOUT in *status (when not null) and leaves NaN in the columns
+// it could not finish.
 bool tt_gemv_fused_y(cudaStream_t s, const float *x, const float *cb, int n_codes,
-                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y);
+                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y,
+                     int *status);
 bool tt_fused_applies(const uint16_t *idx, const float *cb, int K, int N, int n_codes);
 
 extern long long g_launches;   // kernels launched by this process

@@ -121,6 +121,9 @@ struct DSArgs {
     // to every rank's copy of the shared buffers (this rank's own included)
     int rank, world;
     void *const *peers;
+    // bound of every wait (ns of %globaltimer); a wait that runs out sets
+    // ST_WAIT_TIMEOUT and the abort flag
+    unsigned long long wait_ns;
 };
 
 constexpr int DS_MAX_WORLD = 8;
@@ -183,12 +186,12 @@ __device__ __forceinline__ int ld_acquire(const int *p) {
 
 // Wait until *ctr >= target; false on abort or timeout (which raises abort).
 __device__ __forceinline__ bool ds_wait_counter(const int *ctr, int target, int *status,
-                                                int *abort) {
+                                                int *abort, unsigned long long limit) {
     if (ld_acquire(ctr) >= target) return true;
     const unsigned long long t0 = globaltimer();
     while (ld_acquire(ctr) < target) {
         if (ld_acquire(abort)) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit) {
             atomicOr(status, ST_WAIT_TIMEOUT);
             atomicExch(abort, 1);
             return false;
@@ -201,11 +204,12 @@ __device__ __forceinline__ bool ds_wait_counter(const int *ctr, int target, int 
 // mbar_wait for the support warps (producer, table builder): their waits are
 // long, so they sleep between polls instead of taking issue slots from the
 // consumer warps on the same scheduler.
-__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, int *status) {
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, int *status,
+                                               unsigned long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit) {
             if (status) atomicOr(status, ST_WAIT_TIMEOUT);
             return false;
         }
@@ -215,11 +219,12 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, i
 }
 
 // Wait until the stage tag says the stage holds piece `seq`.
-__device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *status) {
+__device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *status,
+                                            unsigned long long limit) {
     if (*tag == seq) return true;
     const unsigned long long t0 = globaltimer();
     while (*tag != seq) {
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit) {
             atomicOr(status, ST_WAIT_TIMEOUT);
             return false;
         }
@@ -231,7 +236,7 @@ __device__ __forceinline__ bool ds_wait_tag(volatile int *tag, int seq, int *sta
 __device__ __forceinline__ bool ds_poll_expired(unsigned long long &t0, const DSArgs &a) {
     const unsigned long long now = globaltimer();
     if (!t0) t0 = now;
-    if (now - t0 <= kWaitLimitNs) return false;
+    if (now - t0 <= a.wait_ns) return false;
     atomicOr(a.status, ST_WAIT_TIMEOUT);
     atomicExch(a.abort, 1);
     return true;
@@ -564,7 +569,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 if (ld_acquire(a.abort)) return;
                 const int slot = q & 1;
                 float *tab = tabs + slot * a.tab_cap;
-                if (q >= 2 && !mbar_wait_idle(&tfree[slot], ((q >> 1) - 1) & 1, a.status)) {
+                if (q >= 2 && !mbar_wait_idle(&tfree[slot], ((q >> 1) - 1) & 1, a.status, a.wait_ns)) {
                     atomicExch(a.abort, 1);
                     return;
                 }
@@ -581,7 +586,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                                   reinterpret_cast<const uint8_t *>(ph.norm_w) + off,
                                   min(32768u, wb - off), rawfull);
                 }
-                if (!mbar_wait_idle(rawfull, q & 1, a.status)) {
+                if (!mbar_wait_idle(rawfull, q & 1, a.status, a.wait_ns)) {
                     atomicExch(a.abort, 1);
                     return;
                 }
@@ -609,7 +614,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     for (int j = DS_NCW * r; j < DS_NCW * r + nr; j++, seq++) {
                         const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
                         const int s = seq % S;
-                        if (seq >= S && !mbar_wait_idle(&empty[s], ((seq / S) - 1) & 1, a.status)) {
+                        if (seq >= S && !mbar_wait_idle(&empty[s], ((seq / S) - 1) & 1, a.status, a.wait_ns)) {
                             atomicExch(a.abort, 1);
                             return;
                         }
@@ -724,7 +729,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             }
             const int slot = q & 1;
             const float *tab = tabs + slot * a.tab_cap;
-            if (!bad && !mbar_wait(&tready[slot], (q >> 1) & 1, a.status)) {
+            if (!bad && !mbar_wait(&tready[slot], (q >> 1) & 1, a.status, a.wait_ns)) {
                 bad = true;
                 atomicExch(a.abort, 1);
             }
@@ -761,8 +766,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 for (int b = 0; b < np; b++) {
                     const int seq = seq_base + r * DS_NCW * np + b * nr + (j - DS_NCW * r);
                     const int s = seq % S;
-                    if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status) ||
-                                 !mbar_wait(&full[s], (seq / S) & 1, a.status))) {
+                    if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status, a.wait_ns) ||
+                                 !mbar_wait(&full[s], (seq / S) & 1, a.status, a.wait_ns))) {
                         bad = true;
                         s_bad = 1;
                         atomicExch(a.abort, 1);
@@ -905,7 +910,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     // this rank to arrive, once every rank's candidates are in
                     const int pl = atomicAdd(a.lm_local, 1);
                     pick = pl == ds_ncta(a, ph.groups_all, a.rank, G) * ep1 - 1 &&
-                           ds_wait_counter(a.done + p, ncta * ep1, a.status, a.abort);
+                           ds_wait_counter(a.done + p, ncta * ep1, a.status, a.abort, a.wait_ns);
                 }
                 if (pick) {
                     // the reference's greedy pick: best = logits[0], then

@@ -510,6 +510,9 @@ struct DecodePlan {
     int logits_slot = -1;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
     std::vector<cudaEvent_t> step_ev;
+    // batched prompt pass: activation arena, grown to the longest prompt seen
+    float *pf_arena = nullptr;
+    size_t pf_cap = 0;   // floats
 };
 
 static void free_plan(DecodePlan *p) {
@@ -518,7 +521,7 @@ static void free_plan(DecodePlan *p) {
     if (p->graph) cudaGraphDestroy(p->graph);
     void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->qkv, p->ctx, p->act, p->logits,
                     p->part, p->counters, p->kc, p->vc, p->cand_v, p->cand_i,
-                    p->st, p->prompt, p->gen, p->status, p->hist};
+                    p->st, p->prompt, p->gen, p->status, p->hist, p->pf_arena};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (float *b : p->dev_norm)
@@ -811,6 +814,13 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.rank = rank;
     a.world = world;
     a.peers = p->d_peers;
+    // every device wait of the step gives up after this long (default 2 s);
+    // KLLM_WAIT_LIMIT_MS shortens it, e.g. for a test that makes one run out
+    a.wait_ns = kWaitLimitNs;
+    if (const char *e = getenv("KLLM_WAIT_LIMIT_MS")) {
+        const long long ms = atoll(e);
+        if (ms > 0 && ms <= 60000) a.wait_ns = (unsigned long long)ms * 1000000ull;
+    }
     p->ds_grid = sms;
     p->ds_stages = S;
     p->ds_smem = smem;
@@ -1197,7 +1207,8 @@ static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
 // and SwiGLU as row kernels -- leaving the KV cache of those positions as
 // the per-token steps would.  The last layer needs only its k and v.  The
 // prompt's last position then runs as a regular decode step, which picks
-// the first token.  Buffers are allocated for the call and freed after it.
+// the first token.  Its activations live in one arena of the plan, grown
+// (once) to the longest prompt seen and freed with the plan.
 static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
     const TemplateInfo &t = p->ti;
     const TapeCtx *ctx = &c->base;
@@ -1208,16 +1219,25 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
         set_error("prefill: %d positions exceed the attention kernel's score buffer", R);
         return false;
     }
-    float *hA = nullptr, *hB = nullptr, *xn = nullptr, *big = nullptr, *qr = nullptr,
-          *cx = nullptr, *act = nullptr;
-    const size_t wide = (size_t)R * std::max({(size_t)nq, (size_t)2 * F, (size_t)H});
-    bool ok = KLLM_CUDA(cudaMallocAsync((void **)&hA, (size_t)R * H * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&hB, (size_t)R * H * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&xn, (size_t)R * H * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&big, wide * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&qr, (size_t)R * qd * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&cx, (size_t)R * qd * 4, s)) &&
-              KLLM_CUDA(cudaMallocAsync((void **)&act, (size_t)R * F * 4, s));
+    // arena: hA, hB, xn [R][H]; big [R][max(nq, 2F, H)]; qr, cx [R][qd];
+    // act [R][F] (every piece a multiple of 4 floats: 16-byte aligned)
+    auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
+    const size_t wide = up4((size_t)R * std::max({(size_t)nq, (size_t)2 * F, (size_t)H}));
+    const size_t rh = up4((size_t)R * H), rq = up4((size_t)R * qd), rf = up4((size_t)R * F);
+    const size_t need = 3 * rh + wide + 2 * rq + rf;
+    if (p->pf_cap < need) {
+        if (p->pf_arena) {
+            if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
+            cudaFree(p->pf_arena);
+        }
+        p->pf_arena = nullptr;
+        p->pf_cap = 0;
+        if (!dalloc(&p->pf_arena, need)) return false;
+        p->pf_cap = need;
+    }
+    float *hA = p->pf_arena, *hB = hA + rh, *xn = hB + rh, *big = xn + rh, *qr = big + wide,
+          *cx = qr + rq, *act = cx + rq;
+    bool ok = true;
     auto gemm = [&](int slot, const float *x, float *y) {
         const Slot &sl = ctx->slots[slot];
         const DevSlot &w = c->ds[slot];
@@ -1256,10 +1276,7 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
         g_launches += 5;
         ok = KLLM_CUDA(cudaGetLastError());
     }
-    ok = ok && KLLM_CUDA(cudaGetLastError());
-    for (float *b : {hA, hB, xn, big, qr, cx, act})
-        if (b) cudaFreeAsync(b, s);
-    return ok;
+    return ok && KLLM_CUDA(cudaGetLastError());
 }
 
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,

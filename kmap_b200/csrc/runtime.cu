@@ -655,7 +655,7 @@ bool run_generic(CtxImpl *c) {
                     return false;
                 }
                 if (!tt_gemv_fused_y(st, D(c, op->in0), w.d_cb, s1->n_codes, w.d_idx, K, N,
-                                     c->d_part, c->d_counters, D(c, o)))
+                                     c->d_part, c->d_counters, D(c, o), nullptr))
                     return false;
                 break;
             }

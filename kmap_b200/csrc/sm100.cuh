@@ -75,12 +75,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar`; false (and ST_WAIT_TIMEOUT in *status)
-// when it did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status) {
+// when it did not complete within `limit` ns.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status,
+                                          unsigned long long limit = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0 = globaltimer();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit) {
             if (status) atomicOr(status, ST_WAIT_TIMEOUT);
             return false;
         }

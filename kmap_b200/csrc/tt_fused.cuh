@@ -157,6 +157,7 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
                 bulk_load(reinterpret_cast<uint8_t *>(cbs) + off,
                           reinterpret_cast<const uint8_t *>(a.cb) + off,
                           (uint32_t)min(32768, cb_bulk - off), cbar);
+            int issued = 0;
             for (int b = 0; b < nbox; b++) {
                 const int s = b % NS;
                 if (b >= NS && !mbar_wait(&empty[s], ((b / NS) - 1) & 1, a.status)) break;
@@ -167,7 +168,14 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
                     const int cx = q == 0 ? col0 : a.F + col0;   // NSUB == 2: gate | up
                     tma_load_2d(dst + q * BR * BW, &tmap, cx, k0 + b * BR, &full[s]);
                 }
+                issued = b + 1;
             }
+            // No copy may still be writing this CTA's shared memory when it
+            // exits (after a wait that gave up, the consumers may leave
+            // early): wait, bounded, for the codebook and the last tiles.
+            mbar_wait(cbar, 0, a.status);
+            for (int b = max(0, issued - NS); b < issued; b++)
+                mbar_wait(&full[b % NS], (b / NS) & 1, a.status);
         }
         return;
     }
@@ -264,6 +272,13 @@ k_tt_fused(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ TTA
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // A wait that gave up (ST_WAIT_TIMEOUT in *a.status) leaves this CTA's
+    // chunk sums incomplete: publish NaN, so the affected columns of y are
+    // NaN rather than plausible wrong numbers.
+    if (!ok) {
+#pragma unroll
+        for (int c = 0; c < CPL; c++) acc[c] = __int_as_float(0x7fffffff);
     }
 
     // ---------------------------------------------------------- epilogue --

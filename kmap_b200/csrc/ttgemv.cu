@@ -21,6 +21,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -159,14 +160,15 @@ static bool launch_g(cudaStream_t s, const TFConfig &c, const CUtensorMap &map, 
     a.stages = std::max(1, std::min(c.stages, nbox));
     size_t smem = tf_smem_bytes<NCW, CPL, BR, NSUB>(a.n_codes, maxlen, a.stages);
     auto kern = k_tt_fused<NCW, CPL, BR, NSUB>;
-    static bool attr_set[64] = {};
+    // per device and instance; concurrent first calls may both set it
+    static std::atomic<bool> attr_set[64] = {};
     int dev = 0;
     if (!KLLM_CUDA(cudaGetDevice(&dev))) return false;
-    if (!attr_set[dev & 63]) {
+    if (!attr_set[dev & 63].load(std::memory_order_acquire)) {
         if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             200 * 1024)))
             return false;
-        attr_set[dev & 63] = true;
+        attr_set[dev & 63].store(true, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tf_blocks(c, a.N, a.F, a.emode), a.T);
@@ -217,7 +219,8 @@ bool tt_fused_applies(const uint16_t *idx, const float *cb, int K, int N, int n_
 // MATMUL_TT and of kllm_tt_gemv): part holds T*N floats, counters
 // tf_blocks() zeros (left zero again).
 bool tt_gemv_fused_y(cudaStream_t s, const float *x, const float *cb, int n_codes,
-                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y) {
+                     const uint16_t *idx, int K, int N, float *part, int *counters, float *y,
+                     int *status) {
     TFConfig c = tf_config(K, N, n_codes, E_Y);
     if (!tf_tma_ok(idx, cb, K, N, n_codes, c)) return false;
     CUtensorMap map;
@@ -234,6 +237,7 @@ bool tt_gemv_fused_y(cudaStream_t s, const float *x, const float *cb, int n_code
     a.part = part;
     a.counters = counters;
     a.y = y;
+    a.status = status;
     return launch_tt_fused(s, c, map, a, false);
 }
 
@@ -263,13 +267,25 @@ struct GemvScratch {
     size_t cap = 0;
     int *counters = nullptr;
     size_t ccap = 0;
+    int *status = nullptr;          // device status word of the fused kernel
+    int *status_host = nullptr;     // pinned copy, refreshed after every launch
 };
 static std::mutex g_scratch_mu;
 static GemvScratch g_scratch[64];
 
-static bool scratch_for(int dev, size_t floats, size_t ncount, float **part, int **counters) {
+static bool scratch_for(int dev, size_t floats, size_t ncount, float **part, int **counters,
+                        int **status, int **status_host) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     GemvScratch &s = g_scratch[dev & 63];
+    if (!s.status) {
+        if (!KLLM_CUDA(cudaMalloc((void **)&s.status, sizeof(int))) ||
+            !KLLM_CUDA(cudaMemset(s.status, 0, sizeof(int))) ||
+            !KLLM_CUDA(cudaHostAlloc((void **)&s.status_host, sizeof(int), cudaHostAllocDefault)))
+            return false;
+        *s.status_host = 0;
+    }
+    *status = s.status;
+    *status_host = s.status_host;
     if (s.cap < floats) {
         if (s.part) cudaFree(s.part);
         s.part = nullptr;
@@ -311,10 +327,26 @@ extern "C" int kllm_tt_gemv(const float *x, int rows, const float *codebook, int
     if (!KLLM_CUDA(cudaGetDevice(&dev))) return -1;
     int T = tt_chunks(K);
     float *part = nullptr;
-    int *counters = nullptr;
-    if (!scratch_for(dev, (size_t)T * rows * N, (size_t)N / 64 + 1, &part, &counters)) return -1;
+    int *counters = nullptr, *status = nullptr, *status_host = nullptr;
+    if (!scratch_for(dev, (size_t)T * rows * N, (size_t)N / 64 + 1, &part, &counters, &status,
+                     &status_host))
+        return -1;
+    // A wait of an earlier call's kernel that gave up (its y columns are
+    // NaN) is reported here, once: the pinned copy of the status word is
+    // refreshed on the stream after every fused launch.
+    if (const int st = *reinterpret_cast<volatile int *>(status_host)) {
+        *reinterpret_cast<volatile int *>(status_host) = 0;
+        cudaMemsetAsync(status, 0, sizeof(int), s);
+        set_error("kllm_tt_gemv: an earlier call's kernel reported status 0x%x (a wait timed "
+                  "out; its y holds NaN)", st);
+        return -1;
+    }
     if (rows == 1 && tf_tma_ok(idx, codebook, K, N, n_codes, tf_config(K, N, n_codes, E_Y)))
-        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, part, counters, y) ? 0 : -1;
+        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, part, counters, y, status) &&
+                       KLLM_CUDA(cudaMemcpyAsync(status_host, status, sizeof(int),
+                                                 cudaMemcpyDeviceToHost, s))
+                   ? 0
+                   : -1;
     if (!tt_gemv_partials(s, x, rows, codebook, n_codes, idx, K, N, part)) return -1;
     if (!tt_reduce_partials(s, part, T, rows, N, y)) return -1;
     return 0;

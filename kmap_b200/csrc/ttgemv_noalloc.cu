@@ -22,8 +22,14 @@
 // Host code may not pass the array's name to a kernel: on the host that
 // name is only a stand-in for the symbol, not a device address.  The first
 // call on a device therefore looks the address up with cudaGetSymbolAddress
-// (with that device current) and keeps it; make that first call before any
-// stream capture starts.
+// (with that device current) and keeps it for the life of the process; make
+// that first call before any stream capture starts, and do not call
+// cudaDeviceReset between calls (the kept address would then be stale).
+//
+// A device wait of the kernel that gives up (it should never: the waits only
+// end copies that never land) sets a status word kept beside the counters
+// and leaves NaN in the affected columns of y, so the failure shows in the
+// output without a host synchronisation.
 #include <mutex>
 
 #include "common.cuh"
@@ -38,10 +44,12 @@ constexpr int kNoAllocCounters = kNoAllocMaxCols / 64 + 64;
 
 static __device__ __align__(256) float g_noalloc_part[kNoAllocChunks * kNoAllocMaxCols];
 static __device__ __align__(256) int g_noalloc_counters[kNoAllocCounters];
+static __device__ int g_noalloc_status;
 
 struct NoAllocScratch {
     float *part = nullptr;
     int *counters = nullptr;
+    int *status = nullptr;
     bool ready = false;
 };
 
@@ -57,11 +65,13 @@ bool scratch_addresses(int dev, NoAllocScratch *out) {
     std::lock_guard<std::mutex> lk(g_mu);
     NoAllocScratch &s = g_dev[dev];
     if (!s.ready) {
-        void *p = nullptr, *q = nullptr;
+        void *p = nullptr, *q = nullptr, *r = nullptr;
         if (!KLLM_CUDA(cudaGetSymbolAddress(&p, g_noalloc_part))) return false;
         if (!KLLM_CUDA(cudaGetSymbolAddress(&q, g_noalloc_counters))) return false;
+        if (!KLLM_CUDA(cudaGetSymbolAddress(&r, g_noalloc_status))) return false;
         s.part = static_cast<float *>(p);
         s.counters = static_cast<int *>(q);
+        s.status = static_cast<int *>(r);
         s.ready = true;
     }
     *out = s;
@@ -93,10 +103,12 @@ extern "C" int kllm_tt_gemv_noalloc(const float *x, const float *codebook, int n
     if (!scratch_addresses(dev, &sc)) return -1;
     // counters must start at zero; an earlier call that was cut short could
     // have left some set
-    if (!KLLM_CUDA(cudaMemsetAsync(sc.counters, 0, sizeof(int) * kNoAllocCounters, s)))
+    if (!KLLM_CUDA(cudaMemsetAsync(sc.counters, 0, sizeof(int) * kNoAllocCounters, s)) ||
+        !KLLM_CUDA(cudaMemsetAsync(sc.status, 0, sizeof(int), s)))
         return -1;
     if (tt_fused_applies(idx, codebook, K, N, n_codes))
-        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, sc.part, sc.counters, y)
+        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, sc.part, sc.counters, y,
+                               sc.status)
                    ? 0
                    : -1;
     const int T = tt_chunks(K);

@@ -180,3 +180,117 @@ int refh_bpe_decode(void *h, const int32_t *ids, int n, int max_bytes,
                       c->special_ids, c->num_special, max_bytes,
                       skip_leading_space, out);
 }
+
+/*
+ * A resumable greedy session over the reference tape: the loop of
+ * refh_greedy_logits (FEED_TOKEN, _tape_runner.c:1658-1708, and the
+ * first-max pick, :1717-1727) cut into calls of a few positions each, so a
+ * benchmark can time the whole prompt + generation workload in bounded
+ * windows.  A session holds the prompt, the KV buffers of every layer and
+ * the position reached; refh_session_run advances it by up to n positions
+ * and returns how many it ran (0 once the workload is complete).
+ */
+typedef struct {
+    ChipCtx *c;
+    int *prompt;
+    int prompt_len, max_new, total, step, tok;
+    int *out;
+    float **kb, **vb;
+} RefhSession;
+
+void *refh_session_create(void *h, const int *prompt, int prompt_len, int max_new)
+{
+    ChipCtx *c = (ChipCtx *)h;
+    RefhSession *s = calloc(1, sizeof *s);
+    s->c = c;
+    s->prompt_len = prompt_len;
+    s->max_new = max_new;
+    s->total = prompt_len + max_new;
+    s->prompt = malloc(sizeof(int) * (prompt_len > 0 ? prompt_len : 1));
+    memcpy(s->prompt, prompt, sizeof(int) * prompt_len);
+    s->out = calloc(max_new > 0 ? max_new : 1, sizeof(int));
+    s->tok = prompt_len > 0 ? prompt[0] : 0;
+    int L = c->num_layers;
+    size_t kvcap = (size_t)c->num_kv_heads * c->head_dim * (s->total > 64 ? s->total : 64);
+    s->kb = calloc(L, sizeof(float *));
+    s->vb = calloc(L, sizeof(float *));
+    for (int l = 0; l < L; l++) {
+        s->kb[l] = calloc(kvcap, sizeof(float));
+        s->vb[l] = calloc(kvcap, sizeof(float));
+    }
+    return s;
+}
+
+/* Run up to n more positions; logits (optional): [n][vocab] rows. */
+int refh_session_run(void *sp, int n, float *logits)
+{
+    RefhSession *s = (RefhSession *)sp;
+    ChipCtx *c = s->c;
+    TapeCtx *ctx = c->ctx;
+    int L = c->num_layers, nkv = c->num_kv_heads, hd = c->head_dim;
+    int H = c->hidden_dim, V = c->vocab_size;
+    int es[2] = {1, H}, rs[2] = {1, hd};
+    int ran = 0;
+    for (; ran < n && s->step < s->total; ran++, s->step++) {
+        int step = s->step;
+        if (step < s->prompt_len) s->tok = s->prompt[step];
+        tape_slot_write(ctx, c->token_embed_slot, c->embed_table + (size_t)s->tok * H, H);
+        tape_slot_set_shape(ctx, c->token_embed_slot, es, 2);
+        tape_slot_write(ctx, c->rope_cos_slot, c->rope_cos + (size_t)step * hd, hd);
+        tape_slot_set_shape(ctx, c->rope_cos_slot, rs, 2);
+        tape_slot_write(ctx, c->rope_sin_slot, c->rope_sin + (size_t)step * hd, hd);
+        tape_slot_set_shape(ctx, c->rope_sin_slot, rs, 2);
+        for (int l = 0; l < L; l++) {
+            int ks[3] = {nkv, step, hd};
+            tape_slot_set_external(ctx, c->kv_in_slots[2 * l], s->kb[l], ks, 3);
+            tape_slot_set_external(ctx, c->kv_in_slots[2 * l + 1], s->vb[l], ks, 3);
+        }
+        tape_run(ctx);
+        for (int l = 0; l < L; l++) {
+            int sz;
+            size_t m = (size_t)nkv * (step + 1) * hd;
+            memcpy(s->kb[l], tape_slot_read(ctx, c->kv_out_slots[2 * l], &sz), m * 4);
+            memcpy(s->vb[l], tape_slot_read(ctx, c->kv_out_slots[2 * l + 1], &sz), m * 4);
+        }
+        int lsz;
+        const float *lg = tape_slot_read(ctx, c->logits_slot, &lsz);
+        const float *row = lg + (lsz - V > 0 ? lsz - V : 0);
+        if (logits) memcpy(logits + (size_t)ran * V, row, (size_t)V * 4);
+        if (step >= s->prompt_len - 1) {
+            int gi = step - (s->prompt_len - 1);
+            if (gi < s->max_new) {
+                float best = row[0];
+                int bi = 0;
+                for (int v = 1; v < V; v++)
+                    if (row[v] > best) { best = row[v]; bi = v; }
+                s->out[gi] = bi;
+                s->tok = bi;
+            }
+        }
+    }
+    return ran;
+}
+
+/* Generated tokens so far (returns their count). */
+int refh_session_tokens(void *sp, int *out, int cap)
+{
+    RefhSession *s = (RefhSession *)sp;
+    int n = s->step - (s->prompt_len - 1);
+    if (n < 0) n = 0;
+    if (n > s->max_new) n = s->max_new;
+    if (n > cap) n = cap;
+    memcpy(out, s->out, sizeof(int) * n);
+    return n;
+}
+
+void refh_session_destroy(void *sp)
+{
+    RefhSession *s = (RefhSession *)sp;
+    if (!s) return;
+    for (int l = 0; l < s->c->num_layers; l++) { free(s->kb[l]); free(s->vb[l]); }
+    free(s->kb);
+    free(s->vb);
+    free(s->prompt);
+    free(s->out);
+    free(s);
+}

@@ -86,6 +86,17 @@ class Ref(_Api):
         L.refh_bpe_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, IP]
         L.refh_bpe_decode.argtypes = [C.c_void_p, IP, C.c_int, C.c_int, C.c_int, C.c_char_p]
         L.compile_chip.argtypes = [C.c_char_p, C.c_int, C.c_char_p]
+        L.refh_session_create.restype = C.c_void_p
+        L.refh_session_create.argtypes = [C.c_void_p, IP, C.c_int, C.c_int]
+        L.refh_session_run.restype = C.c_int
+        L.refh_session_run.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.refh_session_tokens.restype = C.c_int
+        L.refh_session_tokens.argtypes = [C.c_void_p, IP, C.c_int]
+        L.refh_session_destroy.argtypes = [C.c_void_p]
+
+    def session(self, h, prompt, max_new):
+        """A resumable greedy run (refh_session_*): .run(n) advances it."""
+        return RefSession(self, h, prompt, max_new)
 
     # chip-level helpers (the reference's own loader and drivers)
     def chip(self, path):
@@ -127,6 +138,33 @@ class Ref(_Api):
         buf = C.create_string_buffer(max_bytes + 256)
         n = self.L.refh_bpe_decode(h, ids.ctypes.data_as(IP), len(ids), max_bytes, skip, buf)
         return buf.raw[:n]
+
+
+class RefSession:
+    """The reference greedy loop cut into windows of positions."""
+
+    def __init__(self, ref: Ref, h, prompt, max_new):
+        self.ref, self.max_new = ref, max_new
+        self.p = np.ascontiguousarray(prompt, np.int32)
+        self.total = len(self.p) + max_new
+        self.s = ref.L.refh_session_create(h, self.p.ctypes.data_as(IP), len(self.p), max_new)
+
+    def run(self, n, logits: np.ndarray | None = None) -> int:
+        ptr = None
+        if logits is not None:
+            assert logits.dtype == np.float32 and logits.flags.c_contiguous and logits.shape[0] >= n
+            ptr = logits.ctypes.data
+        return self.ref.L.refh_session_run(self.s, n, ptr)
+
+    def tokens(self) -> np.ndarray:
+        out = np.zeros(max(self.max_new, 1), np.int32)
+        n = self.ref.L.refh_session_tokens(self.s, out.ctypes.data_as(IP), len(out))
+        return out[:n].copy()
+
+    def close(self):
+        if self.s:
+            self.ref.L.refh_session_destroy(self.s)
+            self.s = None
 
 
 class Oracle(_Api):

@@ -52,7 +52,7 @@ def test_op_vs_oracle(gpu, oracle, case):
 @pytest.mark.parametrize("K,N,codes,rows", [
     (1, 1, 1, 1), (1, 5, 3, 1), (127, 33, 17, 1), (128, 8, 64, 1), (1000, 37, 400, 2),
     (1023, 8, 4096, 1), (1024, 100, 4096, 1), (1025, 9, 5461, 3), (2048, 2560, 4494, 1),
-    (2048, 2048, 4096, 1), (5632, 2048, 5461, 1), (2048, 11264, 5182, 1), (777, 4099, 65536, 1),
+    (2048, 2048, 4096, 1), (2048, 5632, 5461, 1), (5632, 2048, 5461, 1), (2048, 11264, 5182, 1), (777, 4099, 65536, 1),
     (2048, 32000, 5461, 1), (2048, 64, 4096, 8)])
 def test_tt_gemv_bitexact(gpu, oracle, K, N, codes, rows):
     import kmap_b200

@@ -90,3 +90,28 @@ def test_tiny_decode_vs_reference(ref, oracle, chip_dir, name):
     oc.close()
     assert np.array_equal(toks_o, toks_r)
     np.testing.assert_allclose(lg_o, lg_r, rtol=1e-4, atol=1e-5)
+
+
+def test_reference_session_windows_equal_full_run(ref, chip_dir):
+    """The windowed reference session (the benchmark's reference arm) runs
+    the same greedy loop as processor_infer: cut into windows of 5 positions
+    it gives the same tokens and the same logits bits."""
+    path = chip_dir("gqa")
+    h, info = ref.chip(path)
+    V = int(info[0])
+    prompt = np.random.default_rng(8).integers(3, V, 7)
+    toks_r = ref.infer(h, prompt, 16)
+    toks_l, lg_r = ref.greedy_logits(h, prompt, 16, V)
+    s = ref.session(h, prompt, 16)
+    rows = []
+    while True:
+        buf = np.zeros((5, V), np.float32)
+        n = s.run(5, buf)
+        if n == 0:
+            break
+        rows.append(buf[:n])
+    toks_s = s.tokens()
+    s.close()
+    ref.L.refh_chip_destroy(h)
+    assert np.array_equal(toks_s, toks_r)
+    assert np.array_equal(np.concatenate(rows).view(np.uint32), lg_r.view(np.uint32))

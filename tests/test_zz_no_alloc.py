@@ -67,3 +67,27 @@ def test_noalloc_rejects_more_columns_than_its_scratch():
     assert rc != 0
     assert "65536" in (kmap_b200.last_error() or "")
     lib.kllm_clear_error()
+
+
+def test_noalloc_leaves_device_memory_untouched():
+    """After one warm-up call (which looks up the scratch array's address),
+    further calls change neither the device's free memory nor what torch's
+    allocator holds: the entry point allocates nothing."""
+    import torch
+
+    import kmap_b200
+    lib, noalloc = _entry_points()
+    K, N, codes = 2048, 2048, 4096
+    x, cb, idx = _device_case(K, N, codes, 21)
+    y = torch.empty(N, device="cuda")
+    call = lambda: noalloc(x.data_ptr(), cb.data_ptr(), codes, idx.data_ptr(), K, N,
+                           y.data_ptr(), None)
+    assert call() == 0, kmap_b200.last_error()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    held0 = torch.cuda.memory_reserved()
+    for _ in range(5):
+        assert call() == 0, kmap_b200.last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0 and torch.cuda.memory_reserved() == held0
