@@ -462,7 +462,9 @@ def run_ours(args, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
     chip_path = config0_chip(rank)
     order = kmap_b200.ORDER_FAST if args.order == "fast" else kmap_b200.ORDER_EXACT
+    t_open = time.time()
     chip = kmap_b200.Chip(chip_path, order=order)
+    t_open = time.time() - t_open
     shard = world > 1 and not args.replicas
     if shard:   # every rank holds 1/world of the columns; same prompt everywhere
         chip.connect(kmap_b200.exchange_blocks(chip.shard(rank, world)))
@@ -470,8 +472,10 @@ def run_ours(args, rank, world, local_rank):
     p = prompt_ids(seed=0 if shard else rank)
     t0 = time.time()
     chip.infer(p, GEN)      # first call prepares the plan (weights to HBM, graph)
+    t_first = time.time() - t0
     st = chip.stats()
-    log("rank %d: first call %.1fs (fused=%d)" % (rank, time.time() - t0, st["fused"]))
+    log("rank %d: chip open %.2fs, first call %.2fs (fused=%d)" % (rank, t_open, t_first,
+                                                                  st["fused"]))
     for _ in range(max(args.warmup - 1, 0)):
         chip.infer(p, GEN)
 
@@ -556,6 +560,9 @@ def run_ours(args, rank, world, local_rank):
                                      (" x %d GPUs" % world if shard else "") if hbm
                                      else "fallback 6650 GB/s")},
         "clocks": clocks,
+        "load": {"chip_open_s": t_open, "first_call_s": t_first,
+                 "note": "kllm_chip_open (files to host), then the first processor_infer "
+                         "(upload to HBM, decode layouts, graph capture, one 32 + 128 call)"},
     }
     if replicas:
         out["replicas"] = replicas

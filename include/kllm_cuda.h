@@ -167,6 +167,20 @@ int kllm_tt_gemv_host(const float *x, int rows, const float *codebook,
 int kllm_tt_gemm(const float *x, int rows, const float *codebook, int n_codes,
                  const uint16_t *idx, int K, int N, float *y, void *stream);
 
+/* TT-GEMM on the tensor cores (the same product as kllm_tt_gemm, replacing
+ * the per-row MATMUL_TT loop of _tape_runner.c:804-811 for prefill), for
+ * matrices whose codebook entries are all bf16 numbers: x is split into
+ * `terms` (2 or 3) bf16 terms (hi, mid, lo; 3 terms carry all 24 significand
+ * bits of a normal fp32), each weight is exact in bf16, and the products
+ * accumulate in fp32 in tensor memory.  Results agree with kllm_tt_gemm to
+ * fp32 rounding in a different summation order, not bit for bit.  K must be
+ * a multiple of 64 and N of 128; the codebook is checked (a device-to-host
+ * copy) and a codebook with any non-bf16 entry is an error.  Allocates and
+ * frees its bf16 operands on the stream.  Returns 0 or non-zero
+ * (kllm_last_error). */
+int kllm_tt_gemm_tc(const float *x, int rows, const float *codebook, int n_codes,
+                    const uint16_t *idx, int K, int N, float *y, int terms, void *stream);
+
 /* Allocation-free form of kllm_tt_gemv for one row (x is [K], y is [N]).
  * No counterpart in the reference runtime.  For callers that may not
  * allocate device memory -- code running during CUDA graph capture, plugins

@@ -44,6 +44,8 @@ _SIGS = {
                                C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "kllm_tt_gemv_host": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
                                      C.c_int, C.c_int, C.c_void_p]),
+    "kllm_tt_gemm_tc": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                  C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p]),
     "kllm_chip_open": (C.c_void_p, [C.c_char_p]),
     "kllm_chip_close": (None, [C.c_void_p]),
     "kllm_chip_plan_prepare": (C.c_int, [C.c_void_p]),

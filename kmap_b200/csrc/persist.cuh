@@ -124,7 +124,43 @@ struct DSArgs {
     // bound of every wait (ns of %globaltimer); a wait that runs out sets
     // ST_WAIT_TIMEOUT and the abort flag
     unsigned long long wait_ns;
+    // consumer warps that take GEMV tasks (1..8; the others only stage x
+    // and run attention): each task warp holds the ring stage it computes
+    // on, so fewer task warps leave more stages for loads in flight
+    int task_warps;
+    // stages of each task warp's own ring (0: one ring shared by all task
+    // warps, loaded in round order).  With per-warp rings, producer lane w
+    // streams warp w's pieces into stages [w * ring_w, (w + 1) * ring_w) as
+    // soon as one of them is free: a warp's loads never wait behind another
+    // warp's slower consumption, and run ahead across phase boundaries.
+    int ring_w;
+    int kv_prefetch;           // L2 prefetch of the cached k, v rows (0: off)
+#ifdef KLLM_DS_PROFILE
+    // profiling build only: %globaltimer stamps of the step at position
+    // prof_pos, [cta][phase][8] (DS_STAMP slots below)
+    unsigned long long *prof;
+    int prof_pos;
+#endif
 };
+
+// Profiling build (-DKLLM_DS_PROFILE): timestamps of one step, per CTA and
+// phase.  Consumer slots 0 phase start, 1 warp 0's input words in, 2 input
+// staged and normalised (all warps), 3 warp 0's tasks done, 4 phase done
+// (all warps); producer slots 5 first piece issued, 6 last piece issued,
+// 7 ns spent waiting for a free stage; warp 0 slots 8 ns waiting for its
+// pieces to land, 9 ns computing on landed pieces, 10 pieces, 11 pieces it
+// had to wait for.  Compiled out otherwise.
+#ifdef KLLM_DS_PROFILE
+#define DS_STAMP(cond, slot, val)                                                         \
+    do {                                                                                 \
+        if ((cond) && a.prof && a.st->pos == a.prof_pos)                                 \
+            a.prof[((size_t)blockIdx.x * a.nphases + p) * 12 + (slot)] = (val);          \
+    } while (0)
+#else
+#define DS_STAMP(cond, slot, val) \
+    do {                          \
+    } while (0)
+#endif
 
 constexpr int DS_MAX_WORLD = 8;
 // DSArgs::peers, copied into shared memory when a step starts: every
@@ -169,6 +205,7 @@ __device__ __forceinline__ int ds_ncta(const DSArgs &a, int groups_all, int r, i
 }
 
 constexpr int DS_NCW = 8;                    // consumer warps
+constexpr int DS_TCH = 8;                    // K chunks of one warp task (lane = 8 * pair + chunk)
 constexpr int DS_NC = DS_NCW * 32;
 constexpr int DS_PRODUCER = DS_NCW;          // warp: streams the ring
 constexpr int DS_TABLER = DS_NCW + 1;        // warp: builds codebook tables
@@ -563,8 +600,28 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             // The tables, two phases deep, by bulk copy of the replicated
             // table built at upload.
             int q = 0;
+            const int kpos = a.st->pos;
             for (int p = 0; p < a.nphases; p++) {
                 const DSPhase &ph = a.phases[p];
+                if (ph.kind == DS_ATT) {
+                    // this CTA's attention heads read the cached k and v rows
+                    // of their group: into L2 while the QKV phase runs (the
+                    // first head of each group asks for them)
+                    if (lane == 0 && a.kv_prefetch && kpos > 0 && kpos <= a.max_pos)
+                        for (int hq = cta; hq < ph.ntasks; hq += G) {
+                            if (hq % a.groups) continue;
+                            const size_t off = ((size_t)ph.layer * a.nkv + hq / a.groups) *
+                                               a.max_pos * HD;
+                            const uint32_t nb = (uint32_t)kpos * HD * 4;
+                            for (uint32_t o = 0; o < nb; o += 65536) {
+                                prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(a.kc + off) + o,
+                                                 min(65536u, nb - o));
+                                prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(a.vc + off) + o,
+                                                 min(65536u, nb - o));
+                            }
+                        }
+                    continue;
+                }
                 if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
                 if (ld_acquire(a.abort)) return;
                 const int slot = q & 1;
@@ -597,32 +654,96 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             return;
         }
     }
-    if (warp == DS_PRODUCER) {
-        if (lane != 0) return;
-        int seq = 0;   // slot streams, in the consumers' order
+    if (warp == DS_PRODUCER && a.ring_w > 0) {
+        // per-warp rings: lane w feeds task warp w
+        const int NW = a.task_warps, SW = a.ring_w;
+        if (lane >= NW) return;
+        const int w = lane;
         const uint64_t pol = l2_evict_first();
+        int k = 0;   // this warp's piece sequence, across phases
         for (int p = 0; p < a.nphases; p++) {
             const DSPhase &ph = a.phases[p];
             if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
             if (ld_acquire(a.abort)) return;
             const int W = ph.d.W;
             const int J = (ph.ntasks - cta + G - 1) / G * W, ns = ph.d.ns, np = ph.npieces;
-            for (int r = 0; DS_NCW * r < J; r++) {
-                const int nr = min(DS_NCW, J - DS_NCW * r);
+#ifdef KLLM_DS_PROFILE
+            unsigned long long pw = 0;
+            bool first = true;
+#endif
+            for (int j = w; j < J; j += NW) {
+                const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
+                for (int b = 0; b < np; b++, k++) {
+                    const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
+                    const int s = w * SW + k % SW;
+#ifdef KLLM_DS_PROFILE
+                    const unsigned long long tw = globaltimer();
+#endif
+                    if (k >= SW && !mbar_wait_idle(&empty[s], ((k / SW) - 1) & 1, a.status, a.wait_ns)) {
+                        atomicExch(a.abort, 1);
+                        return;
+                    }
+#ifdef KLLM_DS_PROFILE
+                    const unsigned long long tn = globaltimer();
+                    pw += tn - tw;
+                    DS_STAMP(first && w == 0, 5, tn);
+                    first = false;
+                    DS_STAMP(w == 0, 6, tn);
+                    DS_STAMP(w == 0, 7, pw);
+#endif
+                    stage_seq[s] = k;
+                    mbar_expect_tx(&full[s], bytes);
+                    bulk_load_hint(ring + (size_t)s * DS_STAGE,
+                                   ph.stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
+                                   bytes, &full[s], pol);
+                }
+            }
+        }
+        return;
+    }
+    if (warp == DS_PRODUCER) {
+        if (lane != 0) return;
+        int seq = 0;   // slot streams, in the consumers' order
+        const uint64_t pol = l2_evict_first();
+        const int NW = a.task_warps;
+        for (int p = 0; p < a.nphases; p++) {
+            const DSPhase &ph = a.phases[p];
+            if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
+            if (ld_acquire(a.abort)) return;
+            const int W = ph.d.W;
+            const int J = (ph.ntasks - cta + G - 1) / G * W, ns = ph.d.ns, np = ph.npieces;
+#ifdef KLLM_DS_PROFILE
+            unsigned long long pw = 0;   // ns waiting for free stages in this phase
+            bool first = true;
+#endif
+            for (int r = 0; NW * r < J; r++) {
+                const int nr = min(NW, J - NW * r);
                 for (int b = 0; b < np; b++) {
                     const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
-                    for (int j = DS_NCW * r; j < DS_NCW * r + nr; j++, seq++) {
+                    for (int j = NW * r; j < NW * r + nr; j++, seq++) {
                         const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
                         const int s = seq % S;
+#ifdef KLLM_DS_PROFILE
+                        const unsigned long long tw = globaltimer();
+#endif
                         if (seq >= S && !mbar_wait_idle(&empty[s], ((seq / S) - 1) & 1, a.status, a.wait_ns)) {
                             atomicExch(a.abort, 1);
                             return;
                         }
+#ifdef KLLM_DS_PROFILE
+                        const unsigned long long tn = globaltimer();
+                        pw += tn - tw;
+                        DS_STAMP(first, 5, tn);
+                        first = false;
+                        DS_STAMP(true, 6, tn);
+                        DS_STAMP(true, 7, pw);
+#endif
                         stage_seq[s] = seq;
                         mbar_expect_tx(&full[s], bytes);
                         bulk_load_hint(ring + (size_t)s * DS_STAGE,
                                        ph.stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
                                        bytes, &full[s], pol);
+
                     }
                 }
             }
@@ -660,6 +781,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     ph_ready();
     cbar_sync();
     int seq_base = 0, q = 0;
+    int kw = 0;                                // per-warp rings: this warp's pieces so far
     float lm_v = -INFINITY;                    // this warp's first maximum
     int lm_i = -1;
     bool bad = false;                          // this warp gave up a wait
@@ -671,6 +793,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         const DSPhase &ph = s_ph[p & 1];
         const int ntasks = ph.ntasks, emode = ph.emode;
         ph_fetch(p + 1);
+        DS_STAMP(tid == 0, 0, globaltimer());
         if (cta >= ntasks) {
             ph_ready();
             cbar_sync();
@@ -727,6 +850,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         if (ph.save_x) hsave[wk0 + r] = v[u];
                     }
             }
+            DS_STAMP(tid == 0, 1, globaltimer());
             const int slot = q & 1;
             const float *tab = tabs + slot * a.tab_cap;
             if (!bad && !mbar_wait(&tready[slot], (q >> 1) & 1, a.status, a.wait_ns)) {
@@ -746,32 +870,52 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
             }
             cbar_sync();
+            DS_STAMP(tid == 0, 2, globaltimer());
             if (s_bad) break;   // uniform: every consumer warp leaves together
             // ------------------------------------------------ tasks
-            const int W = d.W, lw = __ffs(W) - 1;   // W is 1, 2, 4 or 8
+            const int W = d.W, lw = __ffs(W) - 1;   // W is 1, 2, 4 or 8 (<= task warps)
             const int J = (ph.ntasks - cta + G - 1) / G * W, ns = d.ns, np = ph.npieces;
             const int nfull = d.base / 8;             // steps inside every chunk
+            const int NW = a.task_warps;
+#ifdef KLLM_DS_PROFILE
+            unsigned long long pf_wait = 0, pf_comp = 0, pf_n = 0, pf_nw = 0;
+#endif
             // warp task j: sub-task w = j % W of group m = j / W; a group's W
-            // sub-tasks sit on W adjacent warps of one round
-            for (int j = warp; j < J; j += DS_NCW) {
-                const int r = j / DS_NCW, nr = min(DS_NCW, J - DS_NCW * r);
+            // sub-tasks sit on W adjacent warps of one round of NW tasks
+            for (int j = warp; warp < NW && j < J; j += NW) {
+                const int r = j / NW, nr = min(NW, J - NW * r);
                 const int m = j >> lw, w = j & (W - 1);
                 const int g = (cta + m * G) * a.world + a.rank;   // the matrix's group
-                const int ch = DS_NCW * w + t;        // this lane's chunk
+                const int ch = DS_TCH * w + t;        // this lane's chunk
                 const int len = d.chunk_len(ch);
                 const float *xr = ch < d.T ? xc + ch * xs : xc;
-                const int nch = min(DS_NCW, d.T - DS_NCW * w);   // chunks in this sub-task
+                const int nch = min(DS_TCH, d.T - DS_TCH * w);   // chunks in this sub-task
                 const int n0 = ds_col<HD>(d, g, 2 * cp), n1 = ds_col<HD>(d, g, 2 * cp + 1);
                 float2 acc = make_float2(0.f, 0.f);
                 for (int b = 0; b < np; b++) {
-                    const int seq = seq_base + r * DS_NCW * np + b * nr + (j - DS_NCW * r);
-                    const int s = seq % S;
+                    int seq, s, par;
+                    if (a.ring_w > 0) {   // this warp's own ring
+                        seq = kw++;
+                        s = warp * a.ring_w + seq % a.ring_w;
+                        par = (seq / a.ring_w) & 1;
+                    } else {              // the shared ring, in round order
+                        seq = seq_base + r * NW * np + b * nr + (j - NW * r);
+                        s = seq % S;
+                        par = (seq / S) & 1;
+                    }
+#ifdef KLLM_DS_PROFILE
+                    const unsigned long long tw0 = globaltimer();
+                    const bool landed = mbar_try_wait(&full[s], par);
+#endif
                     if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status, a.wait_ns) ||
-                                 !mbar_wait(&full[s], (seq / S) & 1, a.status, a.wait_ns))) {
+                                 !mbar_wait(&full[s], par, a.status, a.wait_ns))) {
                         bad = true;
                         s_bad = 1;
                         atomicExch(a.abort, 1);
                     }
+#ifdef KLLM_DS_PROFILE
+                    const unsigned long long tl = globaltimer();
+#endif
                     if (!bad) {
                         const uint8_t *st = ring + (size_t)s * DS_STAGE;
                         const int s0 = DS_PIECE_STEPS * b, s1 = min(ns, s0 + DS_PIECE_STEPS);
@@ -783,13 +927,22 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
+#ifdef KLLM_DS_PROFILE
+                    if (warp == 0 && lane == 0) {
+                        const unsigned long long tw2 = globaltimer();
+                        pf_wait += tl - tw0;
+                        pf_comp += tw2 - tl;
+                        pf_n++;
+                        pf_nw += landed ? 0 : 1;
+                    }
+#endif
                 }
                 // chunk sums in chunk order (every lane of the pair gets them)
                 float2 y;
                 y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
                 y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
 #pragma unroll
-                for (int tt = 1; tt < DS_NCW; tt++) {
+                for (int tt = 1; tt < DS_TCH; tt++) {
                     float2 o;
                     o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
                     o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
@@ -857,8 +1010,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
             }
             seq_base += J * np;
+            DS_STAMP(tid == 0, 3, globaltimer());
+#ifdef KLLM_DS_PROFILE
+            DS_STAMP(tid == 0, 8, pf_wait);
+            DS_STAMP(tid == 0, 9, pf_comp);
+            DS_STAMP(tid == 0, 10, pf_n);
+            DS_STAMP(tid == 0, 11, pf_nw);
+#endif
             ph_ready();
             cbar_sync();   // every warp's outputs are stored and the table is free
+            DS_STAMP(tid == 0, 4, globaltimer());
             if (tid == 0) mbar_arrive(&tfree[slot]);
             q++;
             if (emode != DE_LM) continue;
@@ -964,6 +1125,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     }
                     if (bad) s_bad = 1;
                     cbar_sync();
+                    DS_STAMP(tid == 0, 2, globaltimer());
                     if (s_bad) break;
                     // scores: 8 threads per position (HD / 8 dims each, summed in
                     // order, then combined by a fixed butterfly), four
@@ -1061,6 +1223,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
                 ph_ready();
                 cbar_sync();   // qv, knv, sc and pctx are free again
+                DS_STAMP(tid == 0, 4, globaltimer());
             }
             if (s_bad) break;
         }

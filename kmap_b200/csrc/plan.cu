@@ -34,6 +34,7 @@
 #include <set>
 #include <vector>
 
+#include "pfgemm.cuh"
 #include "plan.cuh"
 #include "sm100.cuh"
 #include "tt_fused.cuh"
@@ -488,6 +489,7 @@ struct DecodePlan {
     // persistent step kernel
     bool persist = false;
     int order = 0;                 // KLLM_ORDER_* the layouts were built for
+    int task_warps = 8;            // consumer warps taking GEMV tasks
     int vm = TTX_VSLOT;            // what the device streams hold (TTXVals)
     int ds_grid = 0, ds_stages = 0;
     size_t ds_smem = 0;
@@ -513,6 +515,14 @@ struct DecodePlan {
     // batched prompt pass: activation arena, grown to the longest prompt seen
     float *pf_arena = nullptr;
     size_t pf_cap = 0;   // floats
+    // tensor-core projections: per layer the bf16 weights transposed
+    // ([N][K], 4 per layer: qkv, o, gate_up, down), built at the first pass
+    std::vector<void *> pf_wt;
+    int pf_terms = 0;    // bf16 terms of x (0: the exact FP32 TT-GEMM)
+#ifdef KLLM_DS_PROFILE
+    unsigned long long *prof = nullptr;   // step timestamps (profiling build)
+    size_t prof_n = 0;
+#endif
 };
 
 static void free_plan(DecodePlan *p) {
@@ -521,12 +531,18 @@ static void free_plan(DecodePlan *p) {
     if (p->graph) cudaGraphDestroy(p->graph);
     void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->qkv, p->ctx, p->act, p->logits,
                     p->part, p->counters, p->kc, p->vc, p->cand_v, p->cand_i,
-                    p->st, p->prompt, p->gen, p->status, p->hist, p->pf_arena};
+                    p->st, p->prompt, p->gen, p->status, p->hist, p->pf_arena
+#ifdef KLLM_DS_PROFILE
+                    , p->prof
+#endif
+    };
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (float *b : p->dev_norm)
         if (b) cudaFree(b);
     for (void *b : p->ds_bufs)
+        if (b) cudaFree(b);
+    for (void *b : p->pf_wt)
         if (b) cudaFree(b);
     for (void *b : p->opened)
         if (b) cudaIpcCloseMemHandle(b);
@@ -605,6 +621,9 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     }
     const int vm = modes & (1u << TTX_VBF16) ? TTX_VBF16 : modes & (1u << TTX_VF16) ? TTX_VF16 : TTX_VSLOT;
     p->vm = vm;
+    // GEMV task warps per CTA (KLLM_TASK_WARPS, 1..8)
+    p->task_warps = 6;
+    if (const char *e = getenv("KLLM_TASK_WARPS")) p->task_warps = std::max(1, std::min(DS_NCW, atoi(e)));
     auto kern = ds_kernel(hd, vm);
     cudaFuncAttributes fa = {};
     if (!KLLM_CUDA(cudaFuncGetAttributes(&fa, kern))) return false;
@@ -634,7 +653,8 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         if (p->order == KLLM_ORDER_FAST) {
             const int ng =
                 ((mode == TTX_GATE_UP ? (sl.tt_N / 2 + 3) / 4 : (sl.tt_N + 7) / 8) + world - 1) / world;
-            while (W < 8 && (long long)ng * 2 * W <= (long long)sms * DS_NCW &&
+            while (W < 8 && 2 * W <= p->task_warps &&
+                   (long long)ng * 2 * W <= (long long)sms * p->task_warps &&
                    sl.tt_K % (16 * 8 * W) == 0)
                 W *= 2;
         }
@@ -814,6 +834,16 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.rank = rank;
     a.world = world;
     a.peers = p->d_peers;
+#ifdef KLLM_DS_PROFILE
+    {
+        const size_t n = (size_t)sms * nph * 12;
+        if (!dalloc(&p->prof, n) || !KLLM_CUDA(cudaMemset(p->prof, 0, n * 8))) return false;
+        p->prof_n = n;
+        a.prof = p->prof;
+        const char *e = getenv("KLLM_PROF_POS");
+        a.prof_pos = e ? atoi(e) : 100;
+    }
+#endif
     // every device wait of the step gives up after this long (default 2 s);
     // KLLM_WAIT_LIMIT_MS shortens it, e.g. for a test that makes one run out
     a.wait_ns = kWaitLimitNs;
@@ -821,6 +851,11 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         const long long ms = atoll(e);
         if (ms > 0 && ms <= 60000) a.wait_ns = (unsigned long long)ms * 1000000ull;
     }
+    a.task_warps = p->task_warps;
+    // one ring shared by the task warps unless KLLM_WARP_RINGS=1
+    a.ring_w = env_on("KLLM_WARP_RINGS", false) ? S / p->task_warps : 0;
+    if (a.ring_w == 1) a.ring_w = 0;   // one stage per warp would not double-buffer
+    a.kv_prefetch = env_on("KLLM_KV_PREFETCH", true) ? 1 : 0;
     p->ds_grid = sms;
     p->ds_stages = S;
     p->ds_smem = smem;
@@ -1215,16 +1250,49 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
     const int H = t.H, hd = t.hd, nh = t.nh, nkv = t.nkv, F = t.F, L = t.L;
     const int qd = nh * hd, kvd = nkv * hd, nq = qd + 2 * kvd, mp = p->max_pos;
     if (R <= 0) return true;
-    if ((size_t)(R + 1) * 4 > 200 * 1024) {
+    if (!((hd == 64 || hd == 128) && env_on("KLLM_PREFILL_FLASH", true)) &&
+        (size_t)(R + 1) * 4 > 200 * 1024) {
         set_error("prefill: %d positions exceed the attention kernel's score buffer", R);
         return false;
     }
+    // Tensor-core projections (pfgemm.cu) when every codebook is bf16 (the
+    // plan's value streams are bf16) and the shapes fit; KLLM_PREFILL_TC=0
+    // keeps the exact FP32 TT-GEMM, KLLM_PREFILL_TERMS picks 2 or 3 (the
+    // default) bf16 terms of x.
+    if (p->pf_terms == 0 && p->pf_wt.empty()) {
+        bool tc = env_on("KLLM_PREFILL_TC", true) && p->vm == TTX_VBF16;
+        for (int l = 0; tc && l < L; l++)
+            for (int sl : {t.layers[l].qkv, t.layers[l].o, t.layers[l].gu, t.layers[l].dn})
+                tc = tc && pf_gemm_applies(ctx->slots[sl].tt_K, ctx->slots[sl].tt_N);
+        if (tc) {
+            const char *te = getenv("KLLM_PREFILL_TERMS");
+            const int terms = te && atoi(te) == 2 ? 2 : 3;
+            p->pf_wt.assign((size_t)4 * L, nullptr);
+            for (int l = 0; l < L && tc; l++) {
+                const LayerSlots &ls = t.layers[l];
+                const int mats[4] = {ls.qkv, ls.o, ls.gu, ls.dn};
+                for (int i = 0; i < 4 && tc; i++) {
+                    const Slot &sl = ctx->slots[mats[i]];
+                    const DevSlot &w = c->ds[mats[i]];
+                    void *&wt = p->pf_wt[(size_t)4 * l + i];
+                    tc = KLLM_CUDA(cudaMalloc(&wt, (size_t)sl.tt_K * sl.tt_N * 2)) &&
+                         pf_build_wt(s, w.d_idx, w.d_cb, sl.tt_K, sl.tt_N, wt);
+                }
+            }
+            if (!tc) return false;
+            p->pf_terms = terms;
+        }
+    }
     // arena: hA, hB, xn [R][H]; big [R][max(nq, 2F, H)]; qr, cx [R][qd];
-    // act [R][F] (every piece a multiple of 4 floats: 16-byte aligned)
+    // act [R][F]; the bf16 terms of a projection's x [terms][R][max(H, F, qd)]
+    // (every piece a multiple of 4 floats: 16-byte aligned)
     auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t wide = up4((size_t)R * std::max({(size_t)nq, (size_t)2 * F, (size_t)H}));
     const size_t rh = up4((size_t)R * H), rq = up4((size_t)R * qd), rf = up4((size_t)R * F);
-    const size_t need = 3 * rh + wide + 2 * rq + rf;
+    const size_t rxs = p->pf_terms ? up4(((size_t)p->pf_terms * R *
+                                          std::max({(size_t)H, (size_t)F, (size_t)qd}) + 1) / 2)
+                                   : 0;
+    const size_t need = 3 * rh + wide + 2 * rq + rf + rxs;
     if (p->pf_cap < need) {
         if (p->pf_arena) {
             if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
@@ -1236,24 +1304,40 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
         p->pf_cap = need;
     }
     float *hA = p->pf_arena, *hB = hA + rh, *xn = hB + rh, *big = xn + rh, *qr = big + wide,
-          *cx = qr + rq, *act = cx + rq;
+          *cx = qr + rq, *act = cx + rq, *xs = act + rf;
     bool ok = true;
+    int cur_layer = 0;
     auto gemm = [&](int slot, const float *x, float *y) {
         const Slot &sl = ctx->slots[slot];
         const DevSlot &w = c->ds[slot];
+        if (p->pf_terms) {
+            const LayerSlots &ls = t.layers[cur_layer];
+            const int i = slot == ls.qkv ? 0 : slot == ls.o ? 1 : slot == ls.gu ? 2 : 3;
+            return pf_split(s, x, (long long)R * sl.tt_K, p->pf_terms, xs) &&
+                   pf_gemm_tc(s, xs, p->pf_terms, R, sl.tt_K, p->pf_wt[(size_t)4 * cur_layer + i],
+                              sl.tt_N, y, p->status);
+        }
         return kllm_tt_gemm(x, R, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
     };
     const int ew_blocks = 148 * 8;
-    const size_t att_smem = (size_t)(R + 1) * 4;
-    if (ok && att_smem > 48 * 1024)
-        ok = KLLM_CUDA(cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // attention: the tiled kernel for head dims 64 and 128 (KLLM_PREFILL_FLASH=0:
+    // the row kernel, one block per position and head)
+    const bool flash = (hd == 64 || hd == 128) && env_on("KLLM_PREFILL_FLASH", true);
+    const size_t att_smem = flash ? (hd == 64 ? pf_flash_smem<64>() : pf_flash_smem<128>())
+                                  : (size_t)(R + 1) * 4;
+    if (ok && att_smem > 48 * 1024) {
+        const void *fn = !flash ? (const void *)k_pf_attention
+                         : hd == 64 ? (const void *)k_pf_flash<64> : (const void *)k_pf_flash<128>;
+        ok = KLLM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)att_smem));
+    }
     if (ok) {
         k_pf_embed<<<R, PF_THREADS, 0, s>>>(p->embed, p->prompt, H, hA);
         g_launches++;
     }
     for (int l = 0; ok && l < L; l++) {
         const LayerSlots &ls = t.layers[l];
+        cur_layer = l;
         float *kc = p->kc + (size_t)l * nkv * mp * hd, *vc = p->vc + (size_t)l * nkv * mp * hd;
         k_pf_rmsnorm<<<R, PF_THREADS, 0, s>>>(hA, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
         ok = gemm(ls.qkv, xn, big);
@@ -1261,8 +1345,15 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
         k_pf_rope_kv<<<R, PF_THREADS, 0, s>>>(big, nq, nh, nkv, hd, p->rcos, p->rsin, mp, qr, kc, vc);
         g_launches += 2;
         if (l + 1 == L) break;   // later positions need only this layer's k and v
-        k_pf_attention<<<dim3(R, nh), PF_THREADS, att_smem, s>>>(
-            qr, kc, vc, nh, t.groups, hd, mp, p->scale, cx);
+        if (!flash)
+            k_pf_attention<<<dim3(R, nh), PF_THREADS, att_smem, s>>>(
+                qr, kc, vc, nh, t.groups, hd, mp, p->scale, cx);
+        else if (hd == 64)
+            k_pf_flash<64><<<dim3((R + PFA_BQ - 1) / PFA_BQ, nh), 256, att_smem, s>>>(
+                qr, kc, vc, R, nh, t.groups, mp, p->scale, cx);
+        else
+            k_pf_flash<128><<<dim3((R + PFA_BQ - 1) / PFA_BQ, nh), 256, att_smem, s>>>(
+                qr, kc, vc, R, nh, t.groups, mp, p->scale, cx);
         ok = gemm(ls.o, cx, big);
         if (!ok) break;
         k_pf_add<<<ew_blocks, 256, 0, s>>>(hA, big, (long long)R * H, hB);
@@ -1419,3 +1510,22 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
 }
 
 }  // namespace kllm
+
+#ifdef KLLM_DS_PROFILE
+// Profiling build: copy the decode step's timestamps ([cta][phase][12]) to
+// out; returns the number of values (cta count * phases * 12), -1 without a
+// persistent plan.
+extern "C" int kllm_ds_profile(TapeCtx *ctx, unsigned long long *out, int cap, int *grid,
+                               int *nphases) {
+    using namespace kllm;
+    CtxImpl *c = impl(ctx);
+    DecodePlan *p = c ? c->plan : nullptr;
+    if (!p || !p->persist || !p->prof) return -1;
+    *grid = p->ds_grid;
+    *nphases = (int)p->phases.size();
+    const size_t n = std::min<size_t>(p->prof_n, (size_t)cap);
+    cudaSetDevice(c->device);
+    if (!KLLM_CUDA(cudaMemcpy(out, p->prof, n * 8, cudaMemcpyDeviceToHost))) return -1;
+    return (int)n;
+}
+#endif

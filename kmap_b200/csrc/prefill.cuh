@@ -126,6 +126,135 @@ __global__ void k_pf_attention(const float *__restrict__ q, const float *__restr
     }
 }
 
+// Causal attention of R prompt positions, tiled (flash-style): block =
+// (64 queries, head h); key/value tiles of 64 positions of the head's kv
+// group go through shared memory, scores with fused multiply-adds, an
+// online softmax per query row (running max and sum, exp in float) and the
+// P.V tile product.  A tolerance result like the row kernel above (whose
+// exact-order sums it replaces at long prompts): the decode step and the
+// reference sum in other orders.  (grid: ceil(R / 64) x nh blocks, 256
+// threads, dynamic shared memory pf_flash_smem<HD>())
+constexpr int PFA_BQ = 64, PFA_BK = 64;
+
+template <int HD>
+__host__ __device__ constexpr size_t pf_flash_smem() {
+    return (size_t)4 * (PFA_BQ * (HD + 1) + PFA_BK * (HD + 1) + PFA_BK * HD + PFA_BQ * (PFA_BK + 1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256)
+k_pf_flash(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
+           int R, int nh, int groups, int max_pos, float scale, float *__restrict__ ctx) {
+    constexpr int DQ = HD / 16;                 // output dims per thread (4 or 8)
+    extern __shared__ float sm[];
+    float *Qs = sm;                             // [BQ][HD + 1]
+    float *Ks = Qs + PFA_BQ * (HD + 1);         // [BK][HD + 1]
+    float *Vs = Ks + PFA_BK * (HD + 1);         // [BK][HD]
+    float *Ps = Vs + PFA_BK * HD;               // [BQ][BK + 1]
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int qt = blockIdx.x, h = blockIdx.y, g = h / groups;
+    const int q0 = qt * PFA_BQ, qd = nh * HD;
+    const float *kg = kc + (size_t)g * max_pos * HD;
+    const float *vg = vc + (size_t)g * max_pos * HD;
+    for (int i = tid; i < PFA_BQ * HD; i += 256) {
+        const int r = i / HD, d = i % HD;
+        Qs[r * (HD + 1) + d] = q0 + r < R ? q[(size_t)(q0 + r) * qd + h * HD + d] : 0.f;
+    }
+    float m[4], l[4], o[4][DQ];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DQ; d++) o[i][d] = 0.f;
+    }
+    const int last_q = min(q0 + PFA_BQ, R) - 1;
+    for (int k0 = 0; k0 <= last_q; k0 += PFA_BK) {
+        __syncthreads();   // the previous tile's Ks, Vs, Ps are free
+        for (int i = tid; i < PFA_BK * HD; i += 256) {
+            const int r = i / HD, d = i % HD;
+            const bool in = k0 + r <= last_q;
+            Ks[r * (HD + 1) + d] = in ? kg[(size_t)(k0 + r) * HD + d] : 0.f;
+            Vs[r * HD + d] = in ? vg[(size_t)(k0 + r) * HD + d] : 0.f;
+        }
+        __syncthreads();
+        // scores: rows ty*4 + i, key columns tx + 16 j
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < HD; d++) {
+            float qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qv[i] = Qs[(ty * 4 + i) * (HD + 1) + d];
+#pragma unroll
+            for (int j = 0; j < 4; j++) kv[j] = Ks[(tx + 16 * j) * (HD + 1) + d];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) sc[i][j] = fmaf(qv[i], kv[j], sc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int qi = q0 + ty * 4 + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int kj = k0 + tx + 16 * j;
+                sc[i][j] = kj <= qi ? sc[i][j] * scale : -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[i], mx);
+            const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
+            float rs = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float pj = sc[i][j] == -INFINITY ? 0.f : expf(sc[i][j] - mn);
+                Ps[(ty * 4 + i) * (PFA_BK + 1) + tx + 16 * j] = pj;
+                rs += pj;
+            }
+#pragma unroll
+            for (int off = 8; off; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+            l[i] = l[i] * corr + rs;
+            m[i] = mn;
+#pragma unroll
+            for (int d = 0; d < DQ; d++) o[i][d] *= corr;
+        }
+        __syncthreads();
+        // P.V: rows ty*4 + i, dims tx*DQ .. tx*DQ + DQ - 1
+#pragma unroll 4
+        for (int jj = 0; jj < PFA_BK; jj++) {
+            float vv[DQ];
+#pragma unroll
+            for (int d = 0; d < DQ; d += 4) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(Vs + jj * HD + tx * DQ + d);
+                vv[d] = v4.x;
+                vv[d + 1] = v4.y;
+                vv[d + 2] = v4.z;
+                vv[d + 3] = v4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float pv = Ps[(ty * 4 + i) * (PFA_BK + 1) + jj];
+#pragma unroll
+                for (int d = 0; d < DQ; d++) o[i][d] = fmaf(pv, vv[d], o[i][d]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int qi = q0 + ty * 4 + i;
+        if (qi >= R) continue;
+        const float inv = 1.f / l[i];
+#pragma unroll
+        for (int d = 0; d < DQ; d++) ctx[(size_t)qi * qd + h * HD + tx * DQ + d] = o[i][d] * inv;
+    }
+}
+
 // out = a + b, elementwise (the residual adds)
 __global__ void k_pf_add(const float *__restrict__ a, const float *__restrict__ b, long long n,
                          float *__restrict__ out) {

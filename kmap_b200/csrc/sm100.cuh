@@ -127,6 +127,12 @@ __device__ __forceinline__ void prefetch_l2_keep(const void *p) {
     asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16); no completion to wait for.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // L2 policy for data read once (streamed weights): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first() {
     uint64_t p;

@@ -1,4 +1,4 @@
-"""Column-sharded decode on 2 GPUs (skipped with fewer).
+"""Column-sharded decode on 2, 4 and 8 GPUs (each skipped with fewer).
 
 Every rank multiplies its column groups and stores its results into both
 ranks' activations over NVLink inside the decode kernel; each output
@@ -49,18 +49,14 @@ def _run_sharded(path, prompt, max_new, order, world=2):
     return [out[r] for r in range(world)]
 
 
-@pytest.fixture(scope="module")
-def two_gpus(gpu):
-    import kmap_b200
-    if kmap_b200.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-
-
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("order", ["exact", "fast"])
 @pytest.mark.parametrize("name", ["tl", "tinyllama2"])
-def test_sharded_decode_matches_one_gpu(two_gpus, chip_dir, tmp_path, name, order):
+def test_sharded_decode_matches_one_gpu(gpu, chip_dir, tmp_path, name, order, world):
     import kmap_b200
     from kmap_b200 import chipgen
+    if kmap_b200.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     if name == "tinyllama2":
         spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
         spec.num_layers = 2
@@ -74,7 +70,7 @@ def test_sharded_decode_matches_one_gpu(two_gpus, chip_dir, tmp_path, name, orde
         prompt = np.random.default_rng(5).integers(3, V, 5).astype(np.int32)
         toks1 = chip.infer(prompt, 10)
         lg1 = chip.final_logits()
-    res = _run_sharded(path, prompt, 10, o)
+    res = _run_sharded(path, prompt, 10, o, world)
     for toks, lg in res:
         assert toks == toks1.tolist()
         if order == "exact":
