@@ -84,7 +84,9 @@ struct DSPhase {
     int out_kind;              // DSPeer of the output
     int groups_all;            // column groups of the matrix over all ranks
     int layer;
-    int pad_[3];               // 16-byte multiple: copied into shared memory in 16-byte pieces
+    int csplit;                // 2: the two columns of a lane pair go to two warps
+                               // (phases with few groups per CTA), 1: one warp
+    int pad_[2];               // 16-byte multiple: copied into shared memory in 16-byte pieces
 };
 static_assert(sizeof(DSPhase) % 16 == 0, "DSPhase is copied in 16-byte pieces");
 
@@ -128,13 +130,10 @@ struct DSArgs {
     // and run attention): each task warp holds the ring stage it computes
     // on, so fewer task warps leave more stages for loads in flight
     int task_warps;
-    // stages of each task warp's own ring (0: one ring shared by all task
-    // warps, loaded in round order).  With per-warp rings, producer lane w
-    // streams warp w's pieces into stages [w * ring_w, (w + 1) * ring_w) as
-    // soon as one of them is free: a warp's loads never wait behind another
-    // warp's slower consumption, and run ahead across phase boundaries.
-    int ring_w;
     int kv_prefetch;           // L2 prefetch of the cached k, v rows (0: off)
+    int gpu_scope;             // tagged words at GPU scope (one rank only)
+    int l2_pf;                 // L2 prefetch distance in pieces ahead of the ring loads (0: off)
+    int unroll;                // whole pieces through the unrolled scalar loops
 #ifdef KLLM_DS_PROFILE
     // profiling build only: %globaltimer stamps of the step at position
     // prof_pos, [cta][phase][8] (DS_STAMP slots below)
@@ -147,18 +146,25 @@ struct DSArgs {
 // phase.  Consumer slots 0 phase start, 1 warp 0's input words in, 2 input
 // staged and normalised (all warps), 3 warp 0's tasks done, 4 phase done
 // (all warps); producer slots 5 first piece issued, 6 last piece issued,
-// 7 ns spent waiting for a free stage; warp 0 slots 8 ns waiting for its
-// pieces to land, 9 ns computing on landed pieces, 10 pieces, 11 pieces it
-// had to wait for.  Compiled out otherwise.
+// 7 ns spent waiting for a free stage; warp 0 (SM clock cycles) slots 8
+// waiting for its pieces to land, 9 computing on landed pieces, 10 pieces,
+// 11 pieces it had to wait for, 12 chunk sums and epilogues, 13 slot 2 to
+// slot 3, 15 slot 0 to slot 2; 14 (CTA 0, phase 0) the %globaltimer step.
+// Compiled out otherwise.
 #ifdef KLLM_DS_PROFILE
+// ds_prof_on: set once per role at kernel start (this step is the profiled one)
 #define DS_STAMP(cond, slot, val)                                                         \
     do {                                                                                 \
-        if ((cond) && a.prof && a.st->pos == a.prof_pos)                                 \
-            a.prof[((size_t)blockIdx.x * a.nphases + p) * 12 + (slot)] = (val);          \
+        if ((cond) && ds_prof_on)                                                        \
+            a.prof[((size_t)blockIdx.x * a.nphases + p) * 16 + (slot)] = (val);          \
     } while (0)
+#define DS_PROF_INIT() const bool ds_prof_on = a.prof && a.st->pos == a.prof_pos
 #else
 #define DS_STAMP(cond, slot, val) \
     do {                          \
+    } while (0)
+#define DS_PROF_INIT() \
+    do {               \
     } while (0)
 #endif
 
@@ -181,14 +187,24 @@ __device__ __forceinline__ uint32_t ds_tag(int ep1, int layer) {
     return (uint32_t)ep1 * 256u + (uint32_t)layer;
 }
 
+// Scope of the tagged-word accesses: the GPU when every reader and writer
+// is on this GPU (one rank), the system when peers store over NVLink.
+__shared__ int ds_gpu_scope;
+
 __device__ __forceinline__ void st_ll(ll_t *p, float v, uint32_t tag) {
     const ll_t w = ((ll_t)tag << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    if (ds_gpu_scope)
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    else
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 __device__ __forceinline__ ll_t ld_ll(const ll_t *p) {
     ll_t w;
-    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if (ds_gpu_scope)
+        asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 
@@ -504,6 +520,153 @@ __device__ __forceinline__ float2 ds_steps_full(const uint8_t *pc, int lane, con
     return acc;
 }
 
+// Split groups: one column of the lane's pair (pc points at that column's
+// 512 bytes of each step).  The 8 values of one step's word q, in row order.
+template <int VM>
+__device__ __forceinline__ void ds_half_vals(const float *tab, const uint4 &q, float (&v)[8]) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        if constexpr (VM == TTX_VSLOT) {
+            v[2 * c] = ds_tab(tab, lo16(w[c]));
+            v[2 * c + 1] = ds_tab(tab, hi16(w[c]));
+        } else if constexpr (VM == TTX_VBF16) {
+            v[2 * c] = bf16_lo(w[c]);
+            v[2 * c + 1] = bf16_hi(w[c]);
+        } else {
+            v[2 * c] = f16_lo(w[c]);
+            v[2 * c + 1] = f16_hi(w[c]);
+        }
+    }
+}
+
+struct DSHalfRaw {
+    uint4 q;
+    float4 xa, xb;
+};
+
+__device__ __forceinline__ DSHalfRaw ds_load_half(const uint8_t *lp, const float *xr) {
+    DSHalfRaw r;
+    r.q = *reinterpret_cast<const uint4 *>(lp);
+    r.xa = *reinterpret_cast<const float4 *>(xr);
+    r.xb = *reinterpret_cast<const float4 *>(xr + 4);
+    return r;
+}
+
+// acc = fl(acc + fl(x[k] * w[k])) over the step's 8 rows, in order.
+template <int VM>
+__device__ __forceinline__ float ds_mac_half(const DSHalfRaw &r, const float *tab, float acc) {
+    float v[8];
+    ds_half_vals<VM>(tab, r.q, v);
+    const float xv[8] = {r.xa.x, r.xa.y, r.xa.z, r.xa.w, r.xb.x, r.xb.y, r.xb.z, r.xb.w};
+    float p[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) p[e] = __fmul_rn(xv[e], v[e]);
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc = __fadd_rn(acc, p[e]);
+    return acc;
+}
+
+// Steps [0, n) of a piece, every row inside the lane's chunk, in order; the
+// next two steps' words and x are in flight while the current two are added.
+template <int VM>
+__device__ __forceinline__ float ds_steps_half(const uint8_t *pc, int lane, const float *xr,
+                                               int n, const float *tab, float acc) {
+    const uint8_t *lp = pc + lane * 16;
+    int i = 0;
+    if (n >= 4) {
+        DSHalfRaw a0 = ds_load_half(lp, xr), a1 = ds_load_half(lp + TTX_STEP, xr + 8);
+        for (; i + 4 <= n; i += 4) {
+            const DSHalfRaw b0 = ds_load_half(lp + (i + 2) * TTX_STEP, xr + 8 * i + 16);
+            const DSHalfRaw b1 = ds_load_half(lp + (i + 3) * TTX_STEP, xr + 8 * i + 24);
+            acc = ds_mac_half<VM>(a0, tab, acc);
+            acc = ds_mac_half<VM>(a1, tab, acc);
+            if (i + 6 <= n) {
+                a0 = ds_load_half(lp + (i + 4) * TTX_STEP, xr + 8 * i + 32);
+                a1 = ds_load_half(lp + (i + 5) * TTX_STEP, xr + 8 * i + 40);
+            }
+            acc = ds_mac_half<VM>(b0, tab, acc);
+            acc = ds_mac_half<VM>(b1, tab, acc);
+        }
+    }
+    for (; i < n; i++) acc = ds_mac_half<VM>(ds_load_half(lp + i * TTX_STEP, xr + 8 * i), tab, acc);
+    return acc;
+}
+
+// A whole piece (DS_PIECE_STEPS steps, every row inside the lane's chunk),
+// one column: fully unrolled so the loads are issued ahead of the dependent
+// add chain (scalar adds: the f32x2 add's dependent latency is about twice
+// the scalar one's).
+template <int VM>
+__device__ __forceinline__ float ds_piece_half(const uint8_t *pc, int lane, const float *xr,
+                                               const float *tab, float acc) {
+    const uint8_t *lp = pc + lane * 16;
+    constexpr int AHEAD = 4;
+    DSHalfRaw r[AHEAD];
+#pragma unroll
+    for (int i = 0; i < AHEAD; i++) r[i] = ds_load_half(lp + i * TTX_STEP, xr + 8 * i);
+#pragma unroll
+    for (int i = 0; i < DS_PIECE_STEPS; i++) {
+        const DSHalfRaw cur = r[i % AHEAD];
+        if (i + AHEAD < DS_PIECE_STEPS)
+            r[i % AHEAD] = ds_load_half(lp + (i + AHEAD) * TTX_STEP, xr + 8 * (i + AHEAD));
+        acc = ds_mac_half<VM>(cur, tab, acc);
+    }
+    return acc;
+}
+
+// The same for both columns of the lane's pair, as two scalar chains.
+template <int VM>
+__device__ __forceinline__ float2 ds_piece_full(const uint8_t *pc, int lane, const float *xr,
+                                                const float *tab, float2 acc) {
+    const uint8_t *lp = pc + lane * 16;
+    constexpr int AHEAD = 3;
+    DSRaw r[AHEAD];
+#pragma unroll
+    for (int i = 0; i < AHEAD; i++) r[i] = ds_load_raw(lp + i * TTX_STEP, xr + 8 * i);
+#pragma unroll
+    for (int i = 0; i < DS_PIECE_STEPS; i++) {
+        const DSRaw cur = r[i % AHEAD];
+        if (i + AHEAD < DS_PIECE_STEPS)
+            r[i % AHEAD] = ds_load_raw(lp + (i + AHEAD) * TTX_STEP, xr + 8 * (i + AHEAD));
+        float v0[8], v1[8];
+        {
+            DSHalfRaw h0 = {cur.q0, cur.xa, cur.xb}, h1 = {cur.q1, cur.xa, cur.xb};
+            ds_half_vals<VM>(tab, h0.q, v0);
+            ds_half_vals<VM>(tab, h1.q, v1);
+        }
+        const float xv[8] = {cur.xa.x, cur.xa.y, cur.xa.z, cur.xa.w,
+                             cur.xb.x, cur.xb.y, cur.xb.z, cur.xb.w};
+        float p0[8], p1[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            p0[e] = __fmul_rn(xv[e], v0[e]);
+            p1[e] = __fmul_rn(xv[e], v1[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            acc.x = __fadd_rn(acc.x, p0[e]);
+            acc.y = __fadd_rn(acc.y, p1[e]);
+        }
+    }
+    return acc;
+}
+
+// One step of which only the first `rows` rows (< 8, may be <= 0) are in
+// the lane's chunk (split groups).
+template <int VM>
+__device__ __forceinline__ float ds_step_tail_half(const uint8_t *stp, int lane, const float *xr,
+                                                   int rows, const float *tab, float acc) {
+    if (rows <= 0) return acc;
+    const uint4 q = *reinterpret_cast<const uint4 *>(stp + lane * 16);
+    float v[8];
+    ds_half_vals<VM>(tab, q, v);
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < rows) acc = __fadd_rn(acc, __fmul_rn(xr[e], v[e]));
+    return acc;
+}
+
 // One step of which only the first `rows` rows (< 8, may be <= 0) are in
 // the lane's chunk.
 template <int VM>
@@ -541,6 +704,55 @@ __device__ __forceinline__ int ds_col(const TTXDesc &d, int g, int c) {
     return n < d.N ? n : -1;
 }
 
+// Walks a CTA's weight pieces in the order its producer loads them from the
+// shared ring (phase, task round, piece, task of the round), continuing
+// with the first phase after the last (the next step's weights are the
+// same): the L2 prefetch cursor.
+struct DSPieceCursor {
+    int p = 0, r = 0, b = 0, j = 0, wraps = 0;
+    int J = 0, W = 1, ns = 0, np = 0, nr = 0, NW = 1;
+    const uint8_t *stream = nullptr;
+
+    // the first GEMV phase with work for this CTA at or after `from`
+    __device__ bool enter(const DSArgs &a, int from, int cta, int G) {
+        for (int k = 0; k < a.nphases; k++) {
+            int q = from + k;
+            if (q >= a.nphases) q -= a.nphases;
+            const DSPhase &ph = a.phases[q];
+            if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
+            if (q < from) wraps++;
+            p = q;
+            NW = a.task_warps;
+            W = ph.d.W;
+            J = (ph.ntasks - cta + G - 1) / G * W;
+            ns = ph.d.ns;
+            np = ph.npieces;
+            stream = ph.stream;
+            r = b = j = 0;
+            nr = min(NW, J);
+            return true;
+        }
+        return false;
+    }
+    __device__ const uint8_t *addr(int cta, int G, uint32_t *bytes) const {
+        *bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
+        const int jj = NW * r + j;
+        const size_t gw = (size_t)(cta + (jj / W) * G) * W + (jj % W);
+        return stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP;
+    }
+    __device__ bool next(const DSArgs &a, int cta, int G) {
+        if (++j < nr) return true;
+        j = 0;
+        if (++b < np) return true;
+        b = 0;
+        if (NW * ++r < J) {
+            nr = min(NW, J - NW * r);
+            return true;
+        }
+        return enter(a, p + 1, cta, G);
+    }
+};
+
 // HD: head dim; VM: what the streams hold (TTXVals, the same for every
 // matrix of the step).
 template <int HD, int VM>
@@ -554,6 +766,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     __shared__ __align__(16) float pctx[NPG][HD];
     __shared__ float rcs[2][HD];               // RoPE cos / sin of this position
     __shared__ int s_bad;                      // a consumer warp gave up a wait
+    __shared__ int s_prod;                     // pieces the producer has issued (shared ring)
+    __shared__ int s_prod_done;
     __shared__ __align__(16) DSPhase s_ph[2];  // consumers: this phase's and the next one's
     __shared__ int ri[DS_NCW];
     __shared__ float2 sub_y[DS_NCW][4];        // split groups: each warp's column sums
@@ -580,7 +794,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], 2);   // two arrivals: the pair of warps of a split
+                                       // group, or one warp arriving twice
             stage_seq[s] = -1;
         }
         for (int i = 0; i < 2; i++) {
@@ -590,15 +805,54 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         mbar_init(rawfull, 1);
         mbar_fence_init();
         s_bad = 0;
+        s_prod = 0;
+        s_prod_done = 0;
     }
     for (int i = threadIdx.x; i < DSP_KINDS * a.world; i += blockDim.x) ds_speers[i] = a.peers[i];
+    if (threadIdx.x == 0) ds_gpu_scope = a.world == 1 && a.gpu_scope;
     __syncthreads();
 
     // ================================================================ producer
+    if (warp == DS_TABLER && lane != 0) {
+        // Lanes 1..31: keep the weight pieces up to l2_pf past the producer's
+        // on their way into L2 (plain L2 prefetches, not the copy engine the
+        // ring loads use), so HBM keeps streaming while the ring is full and
+        // the consumers wait for a phase's input.  The cursor runs on into
+        // the next step's first pieces.
+        if (a.l2_pf <= 0) return;
+        DSPieceCursor c;
+        if (!c.enter(a, 0, cta, G)) return;
+        const volatile int *prod = &s_prod;
+        const volatile int *pdone = &s_prod_done;
+        int pf = 0, last = -1;
+        unsigned long long t_last = globaltimer();
+        while (c.wraps <= 1) {
+            const int pr = *prod;
+            const bool done = *pdone != 0;
+            if (pr != last) {
+                last = pr;
+                t_last = globaltimer();
+            }
+            if (pf > pr + a.l2_pf) {   // far enough ahead: wait for the producer
+                if (done || ld_acquire(a.abort) || globaltimer() - t_last > a.wait_ns) break;
+                __nanosleep(256);
+                continue;
+            }
+            if (pf >= max(pr, S)) {    // not loaded yet, nor about to be
+                uint32_t nb;
+                const uint8_t *base = c.addr(cta, G, &nb);
+                for (uint32_t o = (uint32_t)(lane - 1) * 128u; o < nb; o += 31u * 128u)
+                    prefetch_l2_line(base + o);
+            }
+            if (!c.next(a, cta, G)) break;
+            pf++;
+        }
+        return;
+    }
     if (warp == DS_TABLER) {
         {
             // The tables, two phases deep, by bulk copy of the replicated
-            // table built at upload.
+            // table built at upload (lane 0).
             int q = 0;
             const int kpos = a.st->pos;
             for (int p = 0; p < a.nphases; p++) {
@@ -647,62 +901,15 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     atomicExch(a.abort, 1);
                     return;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tready[slot]);
+                mbar_arrive(&tready[slot]);
                 q++;
             }
             return;
         }
     }
-    if (warp == DS_PRODUCER && a.ring_w > 0) {
-        // per-warp rings: lane w feeds task warp w
-        const int NW = a.task_warps, SW = a.ring_w;
-        if (lane >= NW) return;
-        const int w = lane;
-        const uint64_t pol = l2_evict_first();
-        int k = 0;   // this warp's piece sequence, across phases
-        for (int p = 0; p < a.nphases; p++) {
-            const DSPhase &ph = a.phases[p];
-            if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
-            if (ld_acquire(a.abort)) return;
-            const int W = ph.d.W;
-            const int J = (ph.ntasks - cta + G - 1) / G * W, ns = ph.d.ns, np = ph.npieces;
-#ifdef KLLM_DS_PROFILE
-            unsigned long long pw = 0;
-            bool first = true;
-#endif
-            for (int j = w; j < J; j += NW) {
-                const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
-                for (int b = 0; b < np; b++, k++) {
-                    const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
-                    const int s = w * SW + k % SW;
-#ifdef KLLM_DS_PROFILE
-                    const unsigned long long tw = globaltimer();
-#endif
-                    if (k >= SW && !mbar_wait_idle(&empty[s], ((k / SW) - 1) & 1, a.status, a.wait_ns)) {
-                        atomicExch(a.abort, 1);
-                        return;
-                    }
-#ifdef KLLM_DS_PROFILE
-                    const unsigned long long tn = globaltimer();
-                    pw += tn - tw;
-                    DS_STAMP(first && w == 0, 5, tn);
-                    first = false;
-                    DS_STAMP(w == 0, 6, tn);
-                    DS_STAMP(w == 0, 7, pw);
-#endif
-                    stage_seq[s] = k;
-                    mbar_expect_tx(&full[s], bytes);
-                    bulk_load_hint(ring + (size_t)s * DS_STAGE,
-                                   ph.stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
-                                   bytes, &full[s], pol);
-                }
-            }
-        }
-        return;
-    }
     if (warp == DS_PRODUCER) {
         if (lane != 0) return;
+        DS_PROF_INIT();
         int seq = 0;   // slot streams, in the consumers' order
         const uint64_t pol = l2_evict_first();
         const int NW = a.task_warps;
@@ -716,11 +923,12 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             unsigned long long pw = 0;   // ns waiting for free stages in this phase
             bool first = true;
 #endif
-            for (int r = 0; NW * r < J; r++) {
-                const int nr = min(NW, J - NW * r);
+            const int NWt = NW / ph.csplit;   // tasks per round
+            for (int r = 0; NWt * r < J; r++) {
+                const int nr = min(NWt, J - NWt * r);
                 for (int b = 0; b < np; b++) {
                     const uint32_t bytes = (uint32_t)min(DS_PIECE_STEPS, ns - DS_PIECE_STEPS * b) * TTX_STEP;
-                    for (int j = NW * r; j < NW * r + nr; j++, seq++) {
+                    for (int j = NWt * r; j < NWt * r + nr; j++, seq++) {
                         const size_t gw = (size_t)(cta + (j / W) * G) * W + (j % W);
                         const int s = seq % S;
 #ifdef KLLM_DS_PROFILE
@@ -743,11 +951,13 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         bulk_load_hint(ring + (size_t)s * DS_STAGE,
                                        ph.stream + (gw * ns + (size_t)DS_PIECE_STEPS * b) * TTX_STEP,
                                        bytes, &full[s], pol);
+                        *reinterpret_cast<volatile int *>(&s_prod) = seq + 1;
 
                     }
                 }
             }
         }
+        *reinterpret_cast<volatile int *>(&s_prod_done) = 1;
         return;
     }
 
@@ -758,6 +968,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     // and (times a phase's arrivals) the lm_head counter's target.
     const int ep1 = *a.epoch + 1;
     const int pos = a.st->pos;
+    DS_PROF_INIT();
     if (pos < a.max_pos)   // read by the QKV epilogues, after the first barrier
         for (int d = tid; d < HD; d += DS_NC) {
             rcs[0][d] = __ldg(a.rope_cos + (size_t)pos * HD + d);
@@ -781,7 +992,6 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
     ph_ready();
     cbar_sync();
     int seq_base = 0, q = 0;
-    int kw = 0;                                // per-warp rings: this warp's pieces so far
     float lm_v = -INFINITY;                    // this warp's first maximum
     int lm_i = -1;
     bool bad = false;                          // this warp gave up a wait
@@ -794,6 +1004,15 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
         const int ntasks = ph.ntasks, emode = ph.emode;
         ph_fetch(p + 1);
         DS_STAMP(tid == 0, 0, globaltimer());
+#ifdef KLLM_DS_PROFILE
+        const unsigned long long c0 = clock64();
+        if (p == 0 && cta == 0 && tid == 0) {   // the %globaltimer step
+            const unsigned long long g0 = globaltimer();
+            unsigned long long g1 = g0;
+            for (int i = 0; i < 100000 && g1 == g0; i++) g1 = globaltimer();
+            DS_STAMP(true, 14, g1 - g0);
+        }
+#endif
         if (cta >= ntasks) {
             ph_ready();
             cbar_sync();
@@ -878,12 +1097,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             const int nfull = d.base / 8;             // steps inside every chunk
             const int NW = a.task_warps;
 #ifdef KLLM_DS_PROFILE
-            unsigned long long pf_wait = 0, pf_comp = 0, pf_n = 0, pf_nw = 0;
+            unsigned long long pf_wait = 0, pf_comp = 0, pf_n = 0, pf_nw = 0, pf_epi = 0, pf_redo = 0;
+            const unsigned long long c2 = clock64();
 #endif
             // warp task j: sub-task w = j % W of group m = j / W; a group's W
-            // sub-tasks sit on W adjacent warps of one round of NW tasks
-            for (int j = warp; warp < NW && j < J; j += NW) {
-                const int r = j / NW, nr = min(NW, J - NW * r);
+            // sub-tasks sit on W adjacent warps of one round of NWt tasks.  A
+            // split group (csplit 2) has two warps, `half` 0 for the first
+            // column of every lane pair, 1 for the second.
+            const int cs = ph.csplit, NWt = NW / cs, half = warp % cs;
+            for (int j = warp / cs; warp < NWt * cs && j < J; j += NWt) {
+                const int r = j / NWt, nr = min(NWt, J - NWt * r);
                 const int m = j >> lw, w = j & (W - 1);
                 const int g = (cta + m * G) * a.world + a.rank;   // the matrix's group
                 const int ch = DS_TCH * w + t;        // this lane's chunk
@@ -893,18 +1116,10 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 const int n0 = ds_col<HD>(d, g, 2 * cp), n1 = ds_col<HD>(d, g, 2 * cp + 1);
                 float2 acc = make_float2(0.f, 0.f);
                 for (int b = 0; b < np; b++) {
-                    int seq, s, par;
-                    if (a.ring_w > 0) {   // this warp's own ring
-                        seq = kw++;
-                        s = warp * a.ring_w + seq % a.ring_w;
-                        par = (seq / a.ring_w) & 1;
-                    } else {              // the shared ring, in round order
-                        seq = seq_base + r * NW * np + b * nr + (j - NW * r);
-                        s = seq % S;
-                        par = (seq / S) & 1;
-                    }
+                    const int seq = seq_base + r * NWt * np + b * nr + (j - NWt * r);
+                    const int s = seq % S, par = (seq / S) & 1;
 #ifdef KLLM_DS_PROFILE
-                    const unsigned long long tw0 = globaltimer();
+                    const unsigned long long tw0 = clock64();
                     const bool landed = mbar_try_wait(&full[s], par);
 #endif
                     if (!bad && (!ds_wait_tag(stage_seq + s, seq, a.status, a.wait_ns) ||
@@ -914,22 +1129,51 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         atomicExch(a.abort, 1);
                     }
 #ifdef KLLM_DS_PROFILE
-                    const unsigned long long tl = globaltimer();
+                    const unsigned long long tl = clock64();
 #endif
                     if (!bad) {
                         const uint8_t *st = ring + (size_t)s * DS_STAGE;
                         const int s0 = DS_PIECE_STEPS * b, s1 = min(ns, s0 + DS_PIECE_STEPS);
                         const int sf = min(s1, max(s0, nfull));
-                        acc = ds_steps_full<VM>(st, lane, xr + 8 * s0, sf - s0, tab, acc);
-                        for (int sg = sf; sg < s1; sg++)
-                            acc = ds_step_tail<VM>(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
-                                                   len - 8 * sg, tab, acc);
+                        if (cs == 1 && sf - s0 == DS_PIECE_STEPS && a.unroll) {
+                            acc = ds_piece_full<VM>(st, lane, xr + 8 * s0, tab, acc);
+                        } else if (cs == 2 && sf - s0 == DS_PIECE_STEPS && a.unroll) {
+                            acc.x = ds_piece_half<VM>(st + half * 512, lane, xr + 8 * s0, tab, acc.x);
+#ifdef KLLM_DS_PROFILE
+                            if (warp == 0 && ds_prof_on) {   // the same piece again, timed alone
+                                __syncwarp();
+                                const unsigned long long r0 = clock64();
+                                const float again =
+                                    ds_piece_half<VM>(st + half * 512, lane, xr + 8 * s0, tab, 0.f);
+                                __syncwarp();
+                                const unsigned long long r1 = clock64();
+                                if (lane == 0) pf_redo += r1 - r0 + (again == 12345.f ? 1 : 0);
+                            }
+#endif
+                        } else if (cs == 1) {
+                            acc = ds_steps_full<VM>(st, lane, xr + 8 * s0, sf - s0, tab, acc);
+                            for (int sg = sf; sg < s1; sg++)
+                                acc = ds_step_tail<VM>(st + (sg - s0) * TTX_STEP, lane, xr + 8 * sg,
+                                                       len - 8 * sg, tab, acc);
+                        } else {
+                            acc.x = ds_steps_half<VM>(st + half * 512, lane, xr + 8 * s0, sf - s0,
+                                                      tab, acc.x);
+                            for (int sg = sf; sg < s1; sg++)
+                                acc.x = ds_step_tail_half<VM>(st + (sg - s0) * TTX_STEP + half * 512,
+                                                              lane, xr + 8 * sg, len - 8 * sg, tab,
+                                                              acc.x);
+                        }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
+                    if (lane == 0) {   // two arrivals free the stage
+                        if (cs == 2)
+                            mbar_arrive(&empty[s]);
+                        else
+                            mbar_arrive_cnt(&empty[s], 2);
+                    }
 #ifdef KLLM_DS_PROFILE
                     if (warp == 0 && lane == 0) {
-                        const unsigned long long tw2 = globaltimer();
+                        const unsigned long long tw2 = clock64();
                         pf_wait += tl - tw0;
                         pf_comp += tw2 - tl;
                         pf_n++;
@@ -937,16 +1181,29 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     }
 #endif
                 }
+#ifdef KLLM_DS_PROFILE
+                const unsigned long long te0 = clock64();
+#endif
                 // chunk sums in chunk order (every lane of the pair gets them)
                 float2 y;
-                y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
-                y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
+                if (cs == 1) {
+                    y.x = __shfl_sync(0xffffffffu, acc.x, cp * 8);
+                    y.y = __shfl_sync(0xffffffffu, acc.y, cp * 8);
 #pragma unroll
-                for (int tt = 1; tt < DS_TCH; tt++) {
-                    float2 o;
-                    o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
-                    o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
-                    if (tt < nch) y = __fadd2_rn(y, o);
+                    for (int tt = 1; tt < DS_TCH; tt++) {
+                        float2 o;
+                        o.x = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
+                        o.y = __shfl_sync(0xffffffffu, acc.y, cp * 8 + tt);
+                        if (tt < nch) y = __fadd2_rn(y, o);
+                    }
+                } else {   // this warp's column of every pair, in both halves of y
+                    float v = __shfl_sync(0xffffffffu, acc.x, cp * 8);
+#pragma unroll
+                    for (int tt = 1; tt < DS_TCH; tt++) {
+                        const float o = __shfl_sync(0xffffffffu, acc.x, cp * 8 + tt);
+                        if (tt < nch) v = __fadd_rn(v, o);
+                    }
+                    y = make_float2(v, v);
                 }
                 if (W > 1) {   // sub-task sums of the group, in w order
                     const int bar_id = 2 + warp / W;
@@ -957,8 +1214,9 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(32 * W) : "memory");
                     if (w != 0) continue;   // the group's first warp stores the result
                 }
-                // Epilogue: lane t = k of each pair stores column k of it.
-                const int ek = t;                     // 0, 1: this lane's column
+                // Epilogue: lane t = k of each pair stores column k of it (a
+                // split group: lane t = 0 stores this warp's column).
+                const int ek = cs == 1 ? t : (t == 0 ? half : 2);   // 2: no column
                 const int n = ek ? n1 : n0;
                 const float yk = ek ? y.y : y.x;
                 if (ph.emode == DE_QKV) {
@@ -1008,14 +1266,24 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         }
                     }
                 }
+#ifdef KLLM_DS_PROFILE
+                if (warp == 0) pf_epi += clock64() - te0;
+#endif
             }
             seq_base += J * np;
+#ifdef KLLM_DS_PROFILE
+            const unsigned long long c3 = clock64();
+#endif
             DS_STAMP(tid == 0, 3, globaltimer());
 #ifdef KLLM_DS_PROFILE
             DS_STAMP(tid == 0, 8, pf_wait);
             DS_STAMP(tid == 0, 9, pf_comp);
             DS_STAMP(tid == 0, 10, pf_n);
             DS_STAMP(tid == 0, 11, pf_nw);
+            DS_STAMP(tid == 0, 12, pf_epi);
+            DS_STAMP(tid == 0, 13, c3 - c2);
+            DS_STAMP(tid == 0, 15, c2 - c0);
+            if (p > 0) DS_STAMP(tid == 0, 14, pf_redo);
 #endif
             ph_ready();
             cbar_sync();   // every warp's outputs are stored and the table is free

@@ -725,6 +725,10 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         if (std::min(sms, local_groups(4 * l + 1)) > std::min(sms, local_groups(4 * l)) ||
             std::min(sms, local_groups(4 * l + 3)) > std::min(sms, local_groups(4 * l + 2)))
             return false;
+    // KLLM_COL_SPLIT: 0 never, 1 (default) phases with few groups per CTA,
+    // 2 every phase of the reference order
+    int split_mode = 1;
+    if (const char *e = getenv("KLLM_COL_SPLIT")) split_mode = std::max(0, std::min(2, atoi(e)));
     auto gemv = [&](int mi, int xmode, const ll_t *x, const float *nw, float eps, int emode,
                     int save_x, float *out, int out_kind, int layer, int x_layer) {
         const TTXDesc &d = desc[mi];
@@ -749,6 +753,13 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         m.out_kind = out_kind;
         m.groups_all = groups_all[mi];
         m.layer = layer;
+        // a group's two columns per lane on two warps when the phase has few
+        // groups per CTA (the reference order per column is unchanged)
+        const int per_cta = (d.ngroups + sms - 1) / sms * d.W;
+        m.csplit = split_mode && d.W == 1 &&
+                           (split_mode == 2 || (emode != DE_LM && 2 * per_cta <= p->task_warps))
+                       ? 2
+                       : 1;
         ph.push_back(m);
         return (int)ph.size() - 1;
     };
@@ -836,7 +847,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.peers = p->d_peers;
 #ifdef KLLM_DS_PROFILE
     {
-        const size_t n = (size_t)sms * nph * 12;
+        const size_t n = (size_t)sms * nph * 16;
         if (!dalloc(&p->prof, n) || !KLLM_CUDA(cudaMemset(p->prof, 0, n * 8))) return false;
         p->prof_n = n;
         a.prof = p->prof;
@@ -852,10 +863,11 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
         if (ms > 0 && ms <= 60000) a.wait_ns = (unsigned long long)ms * 1000000ull;
     }
     a.task_warps = p->task_warps;
-    // one ring shared by the task warps unless KLLM_WARP_RINGS=1
-    a.ring_w = env_on("KLLM_WARP_RINGS", false) ? S / p->task_warps : 0;
-    if (a.ring_w == 1) a.ring_w = 0;   // one stage per warp would not double-buffer
     a.kv_prefetch = env_on("KLLM_KV_PREFETCH", true) ? 1 : 0;
+    a.gpu_scope = env_on("KLLM_GPU_SCOPE", true) ? 1 : 0;
+    a.unroll = env_on("KLLM_UNROLL", true) ? 1 : 0;
+    a.l2_pf = 0;
+    if (const char *e = getenv("KLLM_L2_PREFETCH")) a.l2_pf = std::max(0, std::min(512, atoi(e)));
     p->ds_grid = sms;
     p->ds_stages = S;
     p->ds_smem = smem;
@@ -1512,8 +1524,8 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
 }  // namespace kllm
 
 #ifdef KLLM_DS_PROFILE
-// Profiling build: copy the decode step's timestamps ([cta][phase][12]) to
-// out; returns the number of values (cta count * phases * 12), -1 without a
+// Profiling build: copy the decode step's timestamps ([cta][phase][16]) to
+// out; returns the number of values (cta count * phases * 16), -1 without a
 // persistent plan.
 extern "C" int kllm_ds_profile(TapeCtx *ctx, unsigned long long *out, int cap, int *grid,
                                int *nphases) {

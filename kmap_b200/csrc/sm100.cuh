@@ -62,6 +62,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// `count` arrivals at once.
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -131,6 +137,11 @@ __device__ __forceinline__ void prefetch_l2_keep(const void *p) {
 // multiple of 16); no completion to wait for.
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Bring the line holding p into L2 (normal eviction priority).
+__device__ __forceinline__ void prefetch_l2_line(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // L2 policy for data read once (streamed weights): evict first.
