@@ -215,10 +215,18 @@ def ttgemm_time(rows, K, N, C, reps):
     dy = torch.empty((rows, N), device=dev)
     s = torch.cuda.current_stream()
     out = {}
-    for name in ("kllm_tt_gemm",):
+    # the tensor-core form needs a codebook of bf16 numbers: the same codes,
+    # each entry rounded to bf16
+    cb16 = (cb.view(np.uint32) & np.uint32(0xffff0000)).view(np.float32)
+    dc16 = torch.from_numpy(np.pad(cb16, (0, (-len(cb16)) % 4))).to(dev)
+    for name in ("kllm_tt_gemm", "kllm_tt_gemm_tc"):
         f = getattr(lib, name)
-        call = lambda: f(dx.data_ptr(), rows, dc.data_ptr(), C, di.data_ptr(), K, N,
-                         dy.data_ptr(), s.cuda_stream)
+        if name == "kllm_tt_gemm_tc":   # (includes building the bf16 weight and x terms)
+            call = lambda: f(dx.data_ptr(), rows, dc16.data_ptr(), C, di.data_ptr(), K, N,
+                             dy.data_ptr(), 3, s.cuda_stream)
+        else:
+            call = lambda: f(dx.data_ptr(), rows, dc.data_ptr(), C, di.data_ptr(), K, N,
+                             dy.data_ptr(), s.cuda_stream)
         assert call() == 0, kmap_b200.last_error()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)

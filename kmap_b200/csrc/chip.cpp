@@ -10,14 +10,18 @@
 //                    id_to_bytes / id_to_offsets
 //   circuit/         tape.bin [n, 276, records], slots.bin [n, {type, ndim,
 //                    shape[8]}], const_<slot>.bin, const_<slot>_codebook.bin,
-//                    const_<slot>_indices.bin
+//                    const_<slot>_indices.bin (mapped read-only, not read: the
+//                    upload copies it to HBM once)
 // and builds the TapeCtx the same way: type 4 -> truth table, type 1 ->
 // external const, types 2/3 -> allocated.  Unlike the reference it checks
 // every size it relies on and fails with an error message instead of exit().
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <fcntl.h>
+#include <sys/mman.h>
 #include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <string>
@@ -38,7 +42,10 @@ struct kllm_chip {
         id_to_offsets;
     int table_size = 0, max_piece_len = 0, bos = 1;
     std::vector<std::vector<float>> fbufs;      // const slots / codebooks
-    std::vector<std::vector<uint16_t>> ibufs;   // index matrices
+    std::vector<std::vector<uint16_t>> ibufs;   // index matrices (empty ones)
+    // index matrices mapped from their files (read by the upload, which
+    // copies them to HBM once; the pages never need a second host copy)
+    std::vector<std::pair<void *, size_t>> maps;
 };
 
 namespace {
@@ -82,6 +89,30 @@ bool read_array(const std::string &path, std::vector<T> &out, size_t expect = (s
     return true;
 }
 
+// Map a file of exactly `expect` bytes read-only; nullptr (error set) otherwise.
+const void *map_file(const std::string &path, size_t expect, std::vector<std::pair<void *, size_t>> &maps) {
+    const int fd = open(path.c_str(), O_RDONLY);
+    if (fd < 0) {
+        set_error("cannot open %s", path.c_str());
+        return nullptr;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0 || (size_t)st.st_size != expect) {
+        close(fd);
+        set_error("%s: %lld bytes, expected %zu", path.c_str(), (long long)st.st_size, expect);
+        return nullptr;
+    }
+    void *p = mmap(nullptr, expect, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) {
+        set_error("cannot map %s", path.c_str());
+        return nullptr;
+    }
+    madvise(p, expect, MADV_SEQUENTIAL | MADV_WILLNEED);
+    maps.push_back({p, expect});
+    return p;
+}
+
 // Integer after "key": (first occurrence), -1 when absent (kllm.c:31-40).
 int json_int(const std::string &j, const std::string &key, size_t from = 0, size_t to = std::string::npos) {
     std::string pat = "\"" + key + "\"";
@@ -111,6 +142,7 @@ extern "C" {
 void kllm_chip_close(kllm_chip *chip) {
     if (!chip) return;
     if (chip->ctx) tape_ctx_destroy(chip->ctx);
+    for (auto &m : chip->maps) munmap(m.first, m.second);
     delete chip;
 }
 
@@ -247,20 +279,26 @@ kllm_chip *kllm_chip_open(const char *dir_c) {
             }
             size_t K = shape[0], N = shape[1];
             std::vector<float> cb;
-            std::vector<uint16_t> ix;
             snprintf(name, sizeof name, "const_%d_codebook.bin", s);
             if (!read_array(circ + name, cb)) return fail();
-            snprintf(name, sizeof name, "const_%d_indices.bin", s);
-            if (!read_array(circ + name, ix, K * N)) return fail();
             if (cb.empty() || cb.size() > 65536) {
                 set_error("slot %d: codebook of %zu entries", s, cb.size());
                 return fail();
             }
+            snprintf(name, sizeof name, "const_%d_indices.bin", s);
+            uint16_t *ix = nullptr;
+            if (K * N) {   // mapped, not read: the upload copies it to HBM once
+                ix = (uint16_t *)map_file(circ + name, K * N * 2, c->maps);
+                if (!ix) return fail();
+            } else {
+                std::vector<uint16_t> e;
+                if (!read_array(circ + name, e, 0)) return fail();
+                c->ibufs.push_back(std::move(e));
+                ix = c->ibufs.back().data();
+            }
             c->fbufs.push_back(std::move(cb));
-            c->ibufs.push_back(std::move(ix));
             tape_slot_set_truth_table(c->ctx, s, c->fbufs.back().data(),
-                                      (int)c->fbufs.back().size(), c->ibufs.back().data(),
-                                      (int)K, (int)N);
+                                      (int)c->fbufs.back().size(), ix, (int)K, (int)N);
         } else if (type == 1) {
             std::vector<float> d;
             snprintf(name, sizeof name, "const_%d.bin", s);

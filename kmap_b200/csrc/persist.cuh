@@ -62,7 +62,7 @@ enum DSPeer : int {
 // 8-byte access.  A reader that sees its tag sees the value: waiting for an
 // input and reading it are one poll, with no counter, fence or second load.
 typedef unsigned long long ll_t;
-enum DSX : int { DX_EMBED = 0, DX_NORM = 1, DX_VEC = 2 };
+enum DSX : int { DX_EMBED = 0, DX_NORM = 1, DX_VEC = 2, DX_ATT = 3 };
 enum DSE : int { DE_QKV = 0, DE_RESID = 1, DE_SWIGLU = 2, DE_LM = 3 };
 
 struct DSPhase {
@@ -134,6 +134,11 @@ struct DSArgs {
     int gpu_scope;             // tagged words at GPU scope (one rank only)
     int l2_pf;                 // L2 prefetch distance in pieces ahead of the ring loads (0: off)
     int unroll;                // whole pieces through the unrolled scalar loops
+    // split attention: up to att_spmax CTAs per head, one more split per
+    // att_split_min positions; partial P.V rows [spmax][qd] and (max, sum)
+    // pairs [spmax][nh][2] as tagged words (this rank's own)
+    ll_t *att_part, *att_ml;
+    int att_spmax, att_split_min;
 #ifdef KLLM_DS_PROFILE
     // profiling build only: %globaltimer stamps of the step at position
     // prof_pos, [cta][phase][8] (DS_STAMP slots below)
@@ -353,6 +358,13 @@ __device__ __forceinline__ float ds_block_sum(float v, float *red) {
     float r = red[0];
     for (int i = 1; i < DS_NCW; i++) r = __fadd_rn(r, red[i]);
     return r;
+}
+
+// Attention splits per head at this position (1 up to att_split_min
+// positions, then one more per att_split_min, at most att_spmax).
+__device__ __forceinline__ int ds_nsplit(const DSArgs &a, int pos) {
+    if (a.att_spmax <= 1) return 1;
+    return min(a.att_spmax, (pos + a.att_split_min) / a.att_split_min);
 }
 
 // Token fed at the current position (-1: outside the vocabulary).
@@ -858,15 +870,22 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             for (int p = 0; p < a.nphases; p++) {
                 const DSPhase &ph = a.phases[p];
                 if (ph.kind == DS_ATT) {
-                    // this CTA's attention heads read the cached k and v rows
-                    // of their group: into L2 while the QKV phase runs (the
-                    // first head of each group asks for them)
-                    if (lane == 0 && a.kv_prefetch && kpos > 0 && kpos <= a.max_pos)
-                        for (int hq = cta; hq < ph.ntasks; hq += G) {
-                            if (hq % a.groups) continue;
-                            const size_t off = ((size_t)ph.layer * a.nkv + hq / a.groups) *
-                                               a.max_pos * HD;
-                            const uint32_t nb = (uint32_t)kpos * HD * 4;
+                    // this CTA's attention tasks read cached k and v rows of
+                    // their head's group, positions [j0, j1) of the split:
+                    // into L2 while the QKV phase runs (the first head of
+                    // each group asks for the rows of the cache, which holds
+                    // positions before kpos)
+                    if (lane == 0 && a.kv_prefetch && kpos > 0 && kpos < a.max_pos) {
+                        const int nsp = ds_nsplit(a, kpos);
+                        for (int tk = cta; tk < ph.ntasks; tk += G) {
+                            const int hq = tk % a.nh, sp = tk / a.nh;
+                            if (sp >= nsp || hq % a.groups) continue;
+                            const int span = (kpos + nsp) / nsp;
+                            const int j0 = sp * span, j1 = min(kpos, j0 + span);   // cached rows only
+                            if (j1 <= j0) continue;
+                            const size_t off = (((size_t)ph.layer * a.nkv + hq / a.groups) *
+                                                    a.max_pos + j0) * HD;
+                            const uint32_t nb = (uint32_t)(j1 - j0) * HD * 4;
                             for (uint32_t o = 0; o < nb; o += 65536) {
                                 prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(a.kc + off) + o,
                                                  min(65536u, nb - o));
@@ -874,6 +893,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                                                  min(65536u, nb - o));
                             }
                         }
+                    }
                     continue;
                 }
                 if (ph.kind != DS_GEMV || cta >= ph.ntasks) continue;
@@ -886,7 +906,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 }
                 if (lane == 0) {   // the table, and the norm weights the prologue reads
                     const uint32_t cb = (uint32_t)ph.table_bytes;
-                    const uint32_t wb = ph.xmode != DX_VEC ? (uint32_t)ph.d.K * 4 : 0u;
+                    const uint32_t wb =
+                        ph.xmode == DX_EMBED || ph.xmode == DX_NORM ? (uint32_t)ph.d.K * 4 : 0u;
                     mbar_expect_tx(rawfull, cb + wb);
                     for (uint32_t off = 0; off < cb; off += 32768)
                         bulk_load(reinterpret_cast<uint8_t *>(tab) + off,
@@ -1028,7 +1049,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             // of L rows, one contiguous range) -- then rmsnorm in place:
             // x * rsqrt(mean(x^2) + eps) * w.  Tagged inputs are polled:
             // the wait for the producing phase and the read are one.
-            const bool norm = xmode != DX_VEC;
+            const bool norm = xmode == DX_EMBED || xmode == DX_NORM;
             const int CH = (d.T + DS_NCW - 1) / DS_NCW;   // chunks per warp
             const int wrows = CH == 1 ? (warp < d.T ? d.chunk_len(warp) : 0) : CH * d.base;
             const int wk0 = CH == 1 ? (warp < d.T ? d.chunk_start(warp) : 0) : warp * CH * d.base;
@@ -1048,6 +1069,29 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                 emb = a.embed + (size_t)tok * K;
             }
             const uint32_t xtag = ds_tag(ep1, ph.x_layer);
+            // Input of O after split attention: per head, M = max of the
+            // splits' maxima, weights w_s = exp(m_s - M) and 1 / sum_s l_s w_s
+            // (shared, in pctx), then each row is sum_s P.V_s w_s / that sum.
+            const int nsp = xmode == DX_ATT ? ds_nsplit(a, pos) : 1;
+            float *atab = &pctx[0][0];                 // [nsp][nh][2] (max, sum)
+            float *awt = atab + 2 * nsp * a.nh;        // [nh][nsp + 1]: weights, 1 / denominator
+            if (nsp > 1) {
+                for (int i = tid; i < 2 * nsp * a.nh && !bad; i += DS_NC)
+                    if (!ll_fetch1(a.att_ml + i, xtag, atab + i, a)) bad = true;
+                cbar_sync();
+                for (int h = tid; h < a.nh; h += DS_NC) {
+                    float M = atab[2 * h];
+                    for (int sp = 1; sp < nsp; sp++) M = fmaxf(M, atab[2 * (sp * a.nh + h)]);
+                    float den = 0.f;
+                    for (int sp = 0; sp < nsp; sp++) {
+                        const float w = (float)exp((double)__fsub_rn(atab[2 * (sp * a.nh + h)], M));
+                        awt[h * (nsp + 1) + sp] = w;
+                        den = __fadd_rn(den, __fmul_rn(atab[2 * (sp * a.nh + h) + 1], w));
+                    }
+                    awt[h * (nsp + 1) + nsp] = __fdiv_rn(1.0f, den);
+                }
+                cbar_sync();
+            }
             float ss = 0.f;
             for (int b0 = 0; b0 < wrows; b0 += 32 * LL_BATCH) {
                 float v[LL_BATCH];
@@ -1056,6 +1100,28 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
 #pragma unroll
                     for (int u = 0; u < LL_BATCH; u++)
                         v[u] = u < nu ? __ldcg(emb + wk0 + b0 + lane + 32 * u) : 0.f;
+                } else if (nsp > 1) {
+                    float num[LL_BATCH], part[LL_BATCH];
+#pragma unroll
+                    for (int u = 0; u < LL_BATCH; u++) num[u] = 0.f;
+                    for (int sp = 0; sp < nsp && !bad; sp++) {
+                        if (!ll_fetch(a.att_part + (size_t)sp * a.qd + wk0 + b0 + lane, nu, xtag,
+                                      part, a)) {
+                            bad = true;
+                            break;
+                        }
+#pragma unroll
+                        for (int u = 0; u < LL_BATCH; u++) {
+                            const int h = (wk0 + b0 + lane + 32 * u) / HD;
+                            if (u < nu)
+                                num[u] = __fadd_rn(num[u], __fmul_rn(part[u], awt[h * (nsp + 1) + sp]));
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < LL_BATCH; u++) {
+                        const int h = (wk0 + b0 + lane + 32 * u) / HD;
+                        v[u] = u < nu ? __fmul_rn(num[u], awt[h * (nsp + 1) + nsp]) : 0.f;
+                    }
                 } else if (!bad && !ll_fetch(ph.x + wk0 + b0 + lane, nu, xtag, v, a)) {
                     bad = true;
                 }
@@ -1379,9 +1445,18 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
             const float *vcl = a.vc + (size_t)l * a.nkv * a.max_pos * HD;
             const ll_t *knl = ds_peer<ll_t>(a, DSP_KN, a.rank);
             const ll_t *vnl = ds_peer<ll_t>(a, DSP_VN, a.rank);
-            for (int hq = cta; hq < ntasks; hq += G) {
+            // Task tk: head tk % nh, split tk / nh.  Up to 256 positions one
+            // split per head (the whole softmax here, ctx words out); longer
+            // contexts go to nsp splits of consecutive positions, each
+            // leaving its max, its sum of exps and its unnormalised P.V
+            // (the O phase's input staging combines them).
+            const int nsp = ds_nsplit(a, pos);
+            for (int tk = cta; tk < ntasks; tk += G) {
+                const int hq = tk % a.nh, sp = tk / a.nh;
                 const int g = hq / a.groups;
-                if (pos < a.max_pos) {
+                const int span = (pos + nsp) / nsp;   // ceil((pos + 1) / nsp)
+                const int j0 = sp * span, j1 = min(pos + 1, j0 + span), n = j1 - j0;
+                if (pos < a.max_pos && sp < nsp && n > 0) {   // uniform in the CTA
                     // q of this head and this position's k and v of its
                     // group (positions before it come from the cache)
                     for (int i = tid; i < 3 * HD && !bad; i += DS_NC) {
@@ -1402,11 +1477,11 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         constexpr int TPP = 8, DQ = NQ / TPP;   // float4 per thread and row
                         const int sub = tid % TPP, pl = tid / TPP;   // 32 position lanes
                         const float4 *q4 = reinterpret_cast<const float4 *>(qv) + sub * DQ;
-                        for (int base = 0; base <= pos; base += 4 * (DS_NC / TPP)) {
+                        for (int base = j0; base < j1; base += 4 * (DS_NC / TPP)) {
                             float4 kk[4][DQ];
 #pragma unroll
                             for (int k = 0; k < 4; k++) {
-                                const int jj = min(base + pl + k * (DS_NC / TPP), pos);
+                                const int jj = min(base + pl + k * (DS_NC / TPP), j1 - 1);
                                 const float4 *kg4 = jj < pos
                                     ? reinterpret_cast<const float4 *>(kcl + ((size_t)g * a.max_pos + jj) * HD)
                                     : reinterpret_cast<const float4 *>(knv[0]);
@@ -1428,26 +1503,27 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                                 dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, 2));
                                 dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, 4));
                                 const int jj = base + pl + k * (DS_NC / TPP);
-                                if (sub == 0 && jj <= pos) sc[jj] = __fmul_rn(dot, a.scale);
+                                if (sub == 0 && jj < j1) sc[jj - j0] = __fmul_rn(dot, a.scale);
                             }
                         }
                     }
                     cbar_sync();
                     float m = -INFINITY;
-                    for (int jj = tid; jj <= pos; jj += DS_NC) m = fmaxf(m, sc[jj]);
+                    for (int jj = tid; jj < n; jj += DS_NC) m = fmaxf(m, sc[jj]);
                     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                     if (lane == 0) red[warp] = m;
                     cbar_sync();
                     float mx = red[0];
                     for (int w2 = 1; w2 < DS_NCW; w2++) mx = fmaxf(mx, red[w2]);
                     float sum = 0.f;
-                    for (int jj = tid; jj <= pos; jj += DS_NC) {
+                    for (int jj = tid; jj < n; jj += DS_NC) {
                         const float e = (float)exp((double)__fsub_rn(sc[jj], mx));
                         sc[jj] = e;
                         sum = __fadd_rn(sum, e);
                     }
                     const float tot = ds_block_sum(sum, red);
-                    for (int jj = tid; jj <= pos; jj += DS_NC) sc[jj] = __fdiv_rn(sc[jj], tot);
+                    if (nsp == 1)
+                        for (int jj = tid; jj < n; jj += DS_NC) sc[jj] = __fdiv_rn(sc[jj], tot);
                     cbar_sync();
                     {   // P.V: thread = (dim quad, position group), 4 positions in flight
                         const int dq = tid % NQ, pg = tid / NQ;
@@ -1459,10 +1535,10 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                         };
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         int jj = pg;
-                        for (; jj + 7 * NPG <= pos; jj += 8 * NPG) {
+                        for (; jj + 7 * NPG < n; jj += 8 * NPG) {
                             float4 vj[8];
 #pragma unroll
-                            for (int e = 0; e < 8; e++) vj[e] = vrow(jj + e * NPG);
+                            for (int e = 0; e < 8; e++) vj[e] = vrow(j0 + jj + e * NPG);
 #pragma unroll
                             for (int e = 0; e < 8; e++) {
                                 const float pj = sc[jj + e * NPG];
@@ -1472,8 +1548,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                                 acc.w = __fadd_rn(acc.w, __fmul_rn(pj, vj[e].w));
                             }
                         }
-                        for (; jj <= pos; jj += NPG) {
-                            const float4 vj = vrow(jj);
+                        for (; jj < n; jj += NPG) {
+                            const float4 vj = vrow(j0 + jj);
                             const float pj = sc[jj];
                             acc.x = __fadd_rn(acc.x, __fmul_rn(pj, vj.x));
                             acc.y = __fadd_rn(acc.y, __fmul_rn(pj, vj.y));
@@ -1486,7 +1562,15 @@ __global__ void __launch_bounds__(DS_THREADS, 1) k_decode_step(const __grid_cons
                     for (int d = tid; d < HD; d += DS_NC) {
                         float acc = pctx[0][d];
                         for (int i2 = 1; i2 < NPG; i2++) acc = __fadd_rn(acc, pctx[i2][d]);
-                        st_ll(a.ctx + hq * HD + d, acc, otag);
+                        if (nsp == 1) {
+                            st_ll(a.ctx + hq * HD + d, acc, otag);
+                        } else {
+                            st_ll(a.att_part + (size_t)sp * a.qd + hq * HD + d, acc, otag);
+                            if (d == 0) {
+                                st_ll(a.att_ml + ((size_t)sp * a.nh + hq) * 2, mx, otag);
+                                st_ll(a.att_ml + ((size_t)sp * a.nh + hq) * 2 + 1, tot, otag);
+                            }
+                        }
                     }
                 }
                 ph_ready();

@@ -711,6 +711,17 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     ll_t *qb = llbuf(qd), *act = llbuf(t.F), *hA = llbuf(H), *hB = llbuf(H);
     ll_t *kn = llbuf(kvd), *vn = llbuf(kvd), *ctxl = llbuf(qd);
     if (!qb || !act || !hA || !hB || !kn || !vn || !ctxl) return false;
+    // Split attention for long contexts: up to att_spmax CTAs per head
+    // (KLLM_ATT_SPLITS; default the CTAs per head the grid allows, at most
+    // 8), one more split every KLLM_ATT_SPLIT_MIN positions (default 256).
+    int att_spmax = std::max(1, std::min(8, sms / std::max(1, t.nh)));
+    if (const char *e = getenv("KLLM_ATT_SPLITS")) att_spmax = std::max(1, std::min(8, atoi(e)));
+    if (att_spmax * t.nh > sms) att_spmax = std::max(1, sms / t.nh);
+    int att_split_min = 256;
+    if (const char *e = getenv("KLLM_ATT_SPLIT_MIN")) att_split_min = std::max(16, atoi(e));
+    if (p->max_pos <= att_split_min) att_spmax = 1;
+    ll_t *att_part = llbuf((size_t)att_spmax * qd), *att_ml = llbuf((size_t)att_spmax * t.nh * 2);
+    if (!att_part || !att_ml) return false;
     if (L > 255) return false;   // ds_tag keeps the layer in 8 bits
     if ((size_t)sms * world > 4096) return false;   // lm_head candidates, one per CTA and rank
     // phases
@@ -772,10 +783,10 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
              p->eps[2 * l], DE_QKV, 1, nullptr, DSP_Q, l, l - 1);
         DSPhase at = {};
         at.kind = DS_ATT;
-        at.ntasks = t.nh;
+        at.ntasks = t.nh * att_spmax;   // task tk: head tk % nh, split tk / nh
         at.layer = l;
         ph.push_back(at);
-        gemv(mq + 1, DX_VEC, ctxl, nullptr, 0.f, DE_RESID, 0, nullptr, DSP_HB, l, l);
+        gemv(mq + 1, DX_ATT, ctxl, nullptr, 0.f, DE_RESID, 0, nullptr, DSP_HB, l, l);
         gemv(mq + 2, DX_NORM, hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], DE_SWIGLU, 1, nullptr,
              DSP_ACT, l, l);
         gemv(mq + 3, DX_VEC, act, nullptr, 0.f, DE_RESID, 0, nullptr, DSP_HA, l, l);
@@ -866,6 +877,10 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     a.kv_prefetch = env_on("KLLM_KV_PREFETCH", true) ? 1 : 0;
     a.gpu_scope = env_on("KLLM_GPU_SCOPE", true) ? 1 : 0;
     a.unroll = env_on("KLLM_UNROLL", true) ? 1 : 0;
+    a.att_part = att_part;
+    a.att_ml = att_ml;
+    a.att_spmax = att_spmax;
+    a.att_split_min = att_split_min;
     a.l2_pf = 0;
     if (const char *e = getenv("KLLM_L2_PREFETCH")) a.l2_pf = std::max(0, std::min(512, atoi(e)));
     p->ds_grid = sms;

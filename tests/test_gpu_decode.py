@@ -134,3 +134,49 @@ def test_tinyllama_width_chip_matches_reference(gpu, ref, tmp_path, order, value
     assert toks_g.tolist() == toks_r.tolist()
     n = len(prompt) + max_new - 1   # the last step's logits are not computed
     np.testing.assert_allclose(lg_g[:n], lg_r[:n], rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("name", ["tl", "gqa", "mha"])
+def test_split_attention_matches_oracle(gpu, oracle, chip_dir, monkeypatch, name):
+    """Attention split over up to 4 CTAs per head once the context passes
+    KLLM_ATT_SPLIT_MIN positions (32 here, 256 by default): each split's
+    max, sum of exps and unnormalised P.V, combined in the O phase's input
+    staging.  Tokens identical to the oracle, logits within 1e-3 / 1e-4."""
+    import kmap_b200
+    monkeypatch.setenv("KLLM_ATT_SPLIT_MIN", "32")
+    path = chip_dir(name)
+    with kmap_b200.Chip(path) as chip:
+        V, S = chip.info["vocab_size"], chip.info["max_seq_len"]
+        prompt = np.random.default_rng(21).integers(3, V, S // 2).astype(np.int32)
+        max_new = S - len(prompt) - 1
+        toks_o, lg_o = _oracle_run(oracle, path, prompt, max_new)
+        toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
+        assert chip.stats()["step_kernel"] == 1
+    assert toks_g.tolist() == toks_o.tolist()
+    np.testing.assert_allclose(lg_g, lg_o, rtol=RTOL, atol=ATOL)
+
+
+def test_long_context_matches_reference(gpu, ref, tmp_path):
+    """700 positions on a 2-layer chip at the TinyLlama-1.1B widths: split
+    attention (3 splits per head at the end) against the compiled reference
+    runtime, token by token."""
+    import kmap_b200
+    from kmap_b200 import chipgen
+    spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
+    spec.num_layers = 2
+    spec.max_seq = 1024
+    path = chipgen.ensure_chip(str(tmp_path), spec)
+    prompt = np.random.default_rng(8).integers(3, spec.vocab_size, 694).astype(np.int32)
+    max_new = 6
+    h, info = ref.chip(path)
+    s = ref.session(h, prompt, max_new)
+    lg_r = np.zeros((len(prompt) + max_new, spec.vocab_size), np.float32)
+    s.run(len(prompt) + max_new, lg_r)
+    toks_r = s.tokens()
+    s.close()
+    ref.L.refh_chip_destroy(h)
+    with kmap_b200.Chip(path) as chip:
+        toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
+    assert toks_g.tolist() == toks_r.tolist()
+    n = len(prompt) + max_new - 1
+    np.testing.assert_allclose(lg_g[:n], lg_r[:n], rtol=RTOL, atol=ATOL)
