@@ -619,6 +619,140 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------- config 3 (7B, decode) --
+
+C3_PROMPT, C3_GEN = 4096, 256
+C3_INDEX_BYTES = 13214154752   # sum of K * N * 2 over the 7B chip's 129 TT matrices
+
+
+def c3_chip(local_rank):
+    """The Llama-2-7B-architecture chip (32 x 4096, 32 MHA heads of 128,
+    SwiGLU 11008, vocab 32000, max_seq 4352), weights drawn on the GPU."""
+    import fcntl
+
+    import torch
+    spec = chipgen.ModelSpec(**{**chipgen.LLAMA2_7B.__dict__})
+    os.makedirs(CHIP_CACHE, exist_ok=True)
+    with open(os.path.join(CHIP_CACHE, ".lock"), "w") as f:
+        fcntl.flock(f, fcntl.LOCK_EX)
+        t = time.time()
+        path = chipgen.ensure_chip(CHIP_CACHE, spec, device=torch.device("cuda", local_rank))
+        log("7B chip ready in %.1fs: %s" % (time.time() - t, path))
+    return path
+
+
+def run_config3(args, rank, world, local_rank):
+    """Config 3: batch-1 greedy decode of 256 tokens after a 4096-token
+    uniform-random prompt on the 7B-architecture chip; the prompt through
+    the batched pass (tensor-core projections), then one decode step kernel
+    per token, column-sharded over the N GPUs for N > 1.  value = generated
+    tokens per second of decode device time; the prompt pass is reported
+    beside it.  Parity: tokens and logits of a shortened run (16 prompt + 8
+    generated) against the compiled reference on the same chip (rank 0)."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    import torch
+    torch.cuda.set_device(local_rank)
+    kmap_b200.lib().kllm_set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local_rank))
+    path = c3_chip(local_rank)
+    if dist:
+        dist.barrier()
+    t_open = time.time()
+    chip = kmap_b200.Chip(path, prefill=True)
+    t_open = time.time() - t_open
+    if world > 1:
+        chip.connect(kmap_b200.exchange_blocks(chip.shard(rank, world)))
+        dist.barrier()
+    V = chip.info["vocab_size"]
+    # parity run first (every rank takes part in a sharded decode)
+    short = np.random.default_rng(5).integers(3, V, 16).astype(np.int32)
+    toks_short = chip.infer(short, 8)
+    lg_short = chip.final_logits()
+    prompt = np.random.default_rng(3).integers(3, V, C3_PROMPT).astype(np.int32)
+    t0 = time.time()
+    chip.infer(prompt, C3_GEN)
+    t_first = time.time() - t0
+    for _ in range(max(args.warmup - 1, 0)):
+        chip.infer(prompt, C3_GEN)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    pre_ms, dec_ms, gen = 0.0, 0.0, 0
+    with Clocks(local_rank) as clk:
+        for _ in range(args.steps):
+            toks = chip.infer(prompt, C3_GEN)
+            st = chip.stats()
+            pre_ms += st["prefill_ms"]
+            dec_ms += st["decode_ms"]
+            gen += len(toks)
+    barrier()
+    tt = torch.tensor([pre_ms, dec_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    pre_ms, dec_ms = tt.tolist()
+    chip.close()
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    # decode_ms covers the 256 generated tokens' steps after the prompt's
+    # last position (plus the final fed token): one kernel per step
+    steps_dec = C3_GEN
+    step_us = dec_ms * 1e3 / (args.steps * steps_dec)
+    gbs = C3_INDEX_BYTES / (step_us * 1e-6) / 1e9
+    hbm = peaks().get("hbm_gbs")
+    out = {"metric": "decode tok/s (generated tokens per second of decode device time)",
+           "value": gen / (dec_ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "higher_is_better": True,
+           "scaling": "strong" if world > 1 else "weak", "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "Llama-2-7B-arch TT chip (32x4096, 32 MHA heads of 128, "
+                      "SwiGLU 11008, vocab 32000, bf16-rounded N(0,0.02) drawn on the GPU), "
+                      "4096-token prompt + 256 greedy tokens, batch 1",
+                      "parallelism": ("column-sharded over %d GPUs" % world if world > 1
+                                      else "single GPU")},
+           "prefill": {"tok_s": args.steps * (C3_PROMPT - 1) / (pre_ms / 1e3),
+                       "ms_per_prompt": pre_ms / args.steps},
+           "roofline": {"bound": "hbm", "kernel": "k_decode_step", "launch_us": step_us,
+                        "algorithmic_bytes_per_launch": C3_INDEX_BYTES, "achieved": gbs,
+                        "peak": hbm * world if hbm else None, "unit": "GB/s",
+                        "frac": gbs / (hbm * world) if hbm else None},
+           "load": {"chip_open_s": t_open, "first_call_s": t_first},
+           "clocks": clk.summary()}
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import harness
+    if harness.have_ref() and not args.no_cpu_baseline:
+        ref = harness.Ref()
+        h, info = ref.chip(path)
+        s = ref.session(h, short, 8)
+        lg = np.zeros((len(short) + 8, V), np.float32)
+        t = time.time()
+        s.run(len(short) + 8, lg)
+        dt = time.time() - t
+        rt = s.tokens()
+        s.close()
+        ref.L.refh_chip_destroy(h)
+        out["parity"] = {"reference": "compiled reference runtime, same chip, 16-token prompt "
+                                      "+ 8 greedy tokens (%.1f s on the host)" % dt,
+                         "tokens_equal": rt.tolist() == toks_short.tolist(),
+                         "final_logits_max_abs_diff": float(np.abs(lg[-1] - lg_short).max()),
+                         "final_logits_allclose_1e-3_1e-4": bool(np.allclose(
+                             lg_short, lg[-1], rtol=1e-4, atol=1e-3))}
+    print(json.dumps(out), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -632,6 +766,9 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="leave the prefill measurement out of the JSON line")
     ap.add_argument("--cpu-sample", metavar="OUT", help=argparse.SUPPRESS)
+    ap.add_argument("--model", default="tinyllama-1.1b", choices=["tinyllama-1.1b", "llama2-7b"],
+                    help="llama2-7b: the 7B-architecture decode workload (4096-token prompt, "
+                         "256 tokens) as its own JSON line")
     ap.add_argument("--order", default="exact", choices=["exact", "fast"],
                     help="TT-GEMV summation order of the decode step: the reference's "
                          "chunked order (bit-identical MATMUL_TT) or the finer split")
@@ -667,7 +804,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.model == "llama2-7b":
+        run_config3(args, rank, world, local_rank)
+    elif args.impl == "reference":
         run_reference_arm(args, rank, world)
     else:
         run_ours(args, rank, world, local_rank)

@@ -168,6 +168,61 @@ class WeightSource:
         return bf16_round(np.float32(1.0) + g)
 
 
+class TorchWeightSource(WeightSource):
+    """Seeded draws on a CUDA device, for chips too large to draw on the
+    host in reasonable time (the 7B/8B architectures): N(0, std) from
+    torch's generator, rounded to bf16 with round-to-nearest-even, -0.0
+    replaced by +0.0.  Same distribution and number format as
+    WeightSource's bf16 draws, different values (another generator)."""
+
+    def __init__(self, spec: ModelSpec, device):
+        super().__init__(spec)
+        if spec.weight_values != "bf16":
+            raise ValueError("the device generator draws bf16 weights only")
+        self.device = device
+
+    def _gen(self, name: str):
+        import torch
+        h = np.frombuffer(name.encode(), dtype=np.uint8).astype(np.uint64)
+        key = int((h * np.uint64(1099511628211)).sum() % np.uint64(2**61 - 1))
+        g = torch.Generator(device=self.device)
+        g.manual_seed((self.spec.seed * 1000003 + key * 31 + len(name)) % (2**63 - 1))
+        return g
+
+    def matrix(self, name: str, rows: int, cols: int):
+        import torch
+        w = torch.randn((rows, cols), generator=self._gen(name), device=self.device,
+                        dtype=torch.float32)
+        w *= float(np.float32(self.spec.weight_std))
+        w = w.to(torch.bfloat16).to(torch.float32)
+        w[w == 0] = 0.0
+        return w
+
+
+def _tt_compress_torch(w):
+    """tt_compress of a bf16-exact float32 CUDA tensor [K][N]: the sorted
+    distinct values and each weight's rank among them (the compiler's rule,
+    kllm_compile.c:778-822), from a histogram of the 16-bit patterns."""
+    global _BF16_ORDER
+    import torch
+    if _BF16_ORDER is None:
+        _BF16_ORDER = _bf16_order()
+    bits = w.contiguous().view(torch.int32)
+    if bool(((bits & 0xFFFF) != 0).any()):
+        raise ValueError("device compression needs bf16-exact weights")
+    hi = ((bits >> 16) & 0xFFFF).to(torch.int64)
+    present = torch.bincount(hi.flatten(), minlength=65536) > 0
+    if bool(present[0x8000]):
+        raise ValueError("-0.0 in the weights")
+    order_all = torch.from_numpy(_BF16_ORDER.astype(np.int64)).to(w.device)
+    order = order_all[present[order_all]]
+    rank = torch.zeros(65536, dtype=torch.int32, device=w.device)
+    rank[order] = torch.arange(order.numel(), dtype=torch.int32, device=w.device)
+    idx = rank[hi].to(torch.int16).cpu().numpy().view(np.uint16)
+    codebook = (order.cpu().numpy().astype(np.uint32) << np.uint32(16)).view(np.float32)
+    return codebook.copy(), idx
+
+
 # ------------------------------------------------------- TT compression --
 
 def _bf16_order() -> np.ndarray:
@@ -462,7 +517,7 @@ def _write(path, data):
 
 
 def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
-                  log=None) -> dict:
+                  log=None, device=None) -> dict:
     """Write a chip for ``spec`` into ``out_dir``; returns a small summary.
 
     With ``write_weights`` the HF-layout ``weights/*.npy`` and
@@ -477,8 +532,19 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
     circuit = os.path.join(out_dir, "circuit")
     for d in ("circuit", "bpe", "tables") + (("weights", "tokenizer") if write_weights else ()):
         os.makedirs(os.path.join(out_dir, d), exist_ok=True)
-    src = WeightSource(spec)
+    src = TorchWeightSource(spec, device) if device is not None else WeightSource(spec)
+    if device is not None and write_weights:
+        raise ValueError("write_weights needs the host generator")
     wdir = os.path.join(out_dir, "weights")
+
+    def cat_t(mats):   # [m.T for m in mats] side by side, host or device
+        if device is None:
+            return np.concatenate([m.T for m in mats], 1)
+        import torch
+        return torch.cat([m.t() for m in mats], 1).contiguous()
+
+    def host(m):
+        return m if device is None else m.cpu().numpy()
     if write_weights:
         with open(os.path.join(wdir, "config.json"), "w") as f:
             json.dump(dict(model_name=c.model_name, num_layers=L, hidden_size=H,
@@ -499,7 +565,7 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
     def tt(wt: np.ndarray):
         nonlocal n_idx_bytes
         K, N = wt.shape
-        res = tt_compress(wt)
+        res = tt_compress(wt) if device is None else _tt_compress_torch(wt)
         if res is None:  # dense fallback, kllm_compile.c:1516-1524
             return const(wt, [K, N]), False
         cb, idx = res
@@ -556,21 +622,21 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
         wv = src.matrix(ln + "v_proj", kv_dim, H)
         for n_, w_ in (("q_proj", wq), ("k_proj", wk), ("v_proj", wv)):
             save_npy(ln + n_ + ".npy", w_)
-        qkv_slot, _ = tt(np.concatenate([wq.T, wk.T, wv.T], 1))
+        qkv_slot, _ = tt(cat_t([wq, wk, wv]))
         del wq, wk, wv
         wo = src.matrix(ln + "o_proj", H, q_dim)
         save_npy(ln + "o_proj.npy", wo)
-        o_slot, _ = tt(wo.T)
+        o_slot, _ = tt(cat_t([wo]))
         del wo
         wg = src.matrix(ln + "gate_proj", F, H)
         wu = src.matrix(ln + "up_proj", F, H)
         save_npy(ln + "gate_proj.npy", wg)
         save_npy(ln + "up_proj.npy", wu)
-        gu_slot, _ = tt(np.concatenate([wg.T, wu.T], 1))
+        gu_slot, _ = tt(cat_t([wg, wu]))
         del wg, wu
         wd = src.matrix(ln + "down_proj", H, F)
         save_npy(ln + "down_proj.npy", wd)
-        d_slot, _ = tt(wd.T)
+        d_slot, _ = tt(cat_t([wd]))
         del wd
         n1 = src.norm(ln + "input_layernorm", H)
         n2 = src.norm(ln + "post_attention_layernorm", H)
@@ -632,7 +698,7 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
     hidden = rms_norm(hidden, fln)
     lm = src.matrix("lm_head", V, H)
     save_npy("lm_head.npy", lm)
-    lm_slot, _ = tt(lm.T)
+    lm_slot, _ = tt(cat_t([lm]))
     del lm
     logits = tb.matmul(T_MATMUL_TT, hidden, lm_slot, [1, V])
 
@@ -661,7 +727,7 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
         with open(os.path.join(out_dir, "tokenizer", "tokenizer_config.json"), "w") as f:
             f.write(tc)
 
-    embed = src.matrix("embed_tokens", V, H)
+    embed = host(src.matrix("embed_tokens", V, H))
     save_npy("embed_tokens.npy", embed)
     tables = os.path.join(out_dir, "tables")
     _write(os.path.join(tables, "embed_table.bin"), embed)
@@ -701,18 +767,22 @@ def generate_chip(out_dir: str, spec: ModelSpec, write_weights: bool = False,
                 index_bytes=n_idx_bytes, logits_slot=logits)
 
 
-def ensure_chip(cache_root: str, spec: ModelSpec, log=None) -> str:
-    """Generate ``spec``'s chip under ``cache_root`` once; return its path."""
+def ensure_chip(cache_root: str, spec: ModelSpec, log=None, device=None) -> str:
+    """Generate ``spec``'s chip under ``cache_root`` once; return its path.
+    With ``device`` (a CUDA device) the weights are drawn there
+    (TorchWeightSource): a different chip, cached under its own name."""
     key = "chip_L%d_H%d_h%d_kv%d_F%d_V%d_S%d_seed%d_%s" % (
         spec.num_layers, spec.hidden_size, spec.num_attention_heads,
         spec.num_key_value_heads, spec.intermediate_size, spec.vocab_size,
         spec.max_seq, spec.seed, spec.norm_weights)
     if spec.weight_values != "bf16":
         key += "_" + spec.weight_values
+    if device is not None:
+        key += "_devrng"
     path = os.path.join(cache_root, key)
     done = os.path.join(path, ".complete")
     if not os.path.exists(done):
-        generate_chip(path, spec, log=log)
+        generate_chip(path, spec, log=log, device=device)
         open(done, "w").close()
     return path
 

@@ -601,6 +601,7 @@ static bool persist_prepare(CtxImpl *c, DecodePlan *p, const std::vector<int> &t
     if (!env_on("KLLM_PERSIST", true)) return false;
     const TapeCtx *ctx = &c->base;
     const TemplateInfo &t = p->ti;
+    if (t.hd != 32 && t.hd != 64 && t.hd != 128) return false;   // the step kernel's instances
     const int H = t.H, hd = t.hd, nkv = t.nkv, qd = t.nh * hd, kvd = nkv * hd;
     const int V = t.V, L = t.L;
     const int nmat = (int)tts.size();
@@ -1459,8 +1460,10 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
     if (!KLLM_CUDA(cudaEventRecord(p->ev0, s))) return false;
     int launched = 0;
     // batched prompt pass for all prompt positions but the last (persistent
-    // single-GPU plan, no per-step logits requested)
-    if (c->opts.prefill && p->persist && p->world == 1 && want_rows == 0 && prompt_len >= 2) {
+    // plan, no per-step logits requested).  A column-sharded rank runs the
+    // whole pass itself from its full matrices: it fills its own copy of the
+    // KV cache, the state every rank holds in full.
+    if (c->opts.prefill && p->persist && want_rows == 0 && prompt_len >= 2) {
         const int R = prompt_len - 1;
         StepState st1 = {R, prompt_len, 0, 0};
         if (!plan_prefill(c, p, R, s) ||

@@ -49,3 +49,38 @@ def test_tinyllama_shapes():
     s = chipgen.TINYLLAMA_1B
     assert (s.num_layers, s.hidden_size, s.head_dim, s.intermediate_size, s.vocab_size) == \
         (22, 2048, 64, 5632, 32000)
+
+
+def test_device_generator_compresses_like_the_host_rule():
+    """The device generation path (TorchWeightSource + the histogram
+    compression, used for the 7B/8B chips) yields bf16 weights and the same
+    codebook and indices as the host tt_compress of the same weights (run
+    here on the CPU device)."""
+    import torch
+
+    from kmap_b200 import chipgen
+    spec = chipgen.ModelSpec(hidden_size=64, intermediate_size=96)
+    src = chipgen.TorchWeightSource(spec, torch.device("cpu"))
+    w = src.matrix("layer_0/q_proj", 96, 64)
+    again = src.matrix("layer_0/q_proj", 96, 64)
+    assert torch.equal(w, again)   # seeded by name
+    wt = torch.cat([w.t()], 1).contiguous()
+    cb_d, idx_d = chipgen._tt_compress_torch(wt)
+    cb_h, idx_h = chipgen.tt_compress(wt.numpy())
+    assert np.array_equal(cb_d.view(np.uint32), cb_h.view(np.uint32))
+    assert np.array_equal(idx_d, idx_h)
+    assert not (wt.numpy().view(np.uint32) & 0xFFFF).any()
+
+
+def test_device_generated_chip_loads(tmp_path):
+    import torch
+
+    import kmap_b200
+    from kmap_b200 import chipgen
+    spec = chipgen.ModelSpec(num_layers=1, hidden_size=64, num_attention_heads=4,
+                             num_key_value_heads=2, intermediate_size=96, vocab_size=300,
+                             max_seq=32)
+    path = chipgen.ensure_chip(str(tmp_path), spec, device=torch.device("cpu"))
+    assert path.endswith("_devrng")
+    with kmap_b200.Chip(path) as chip:
+        assert chip.info["vocab_size"] == 300 and chip.info["num_layers"] == 1

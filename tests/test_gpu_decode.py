@@ -180,3 +180,36 @@ def test_long_context_matches_reference(gpu, ref, tmp_path):
     assert toks_g.tolist() == toks_r.tolist()
     n = len(prompt) + max_new - 1
     np.testing.assert_allclose(lg_g[:n], lg_r[:n], rtol=RTOL, atol=ATOL)
+
+
+HD128 = dict(num_layers=2, hidden_size=512, num_attention_heads=4, num_key_value_heads=2,
+             intermediate_size=1024, vocab_size=1000, max_seq=320, norm_weights="random", seed=9)
+
+
+@pytest.mark.parametrize("mode", ["step", "split", "prefill"])
+def test_head_dim_128_matches_oracle(gpu, oracle, tmp_path, monkeypatch, mode):
+    """Head dim 128 (the 7B / 8B architectures' geometry) through the
+    persistent step kernel's 128 instance: step by step, with attention
+    splits forced (KLLM_ATT_SPLIT_MIN=32), and with the batched prompt pass
+    (tensor-core projections, tiled attention); tokens identical to the
+    oracle, logits within 1e-3 / 1e-4."""
+    import kmap_b200
+    from kmap_b200 import chipgen
+    if mode == "split":
+        monkeypatch.setenv("KLLM_ATT_SPLIT_MIN", "32")
+    path = chipgen.ensure_chip(str(tmp_path), chipgen.ModelSpec(**HD128))
+    prompt = np.random.default_rng(4).integers(3, 1000, 150).astype(np.int32)
+    max_new = 40
+    toks_o, lg_o = _oracle_run(oracle, path, prompt, max_new)
+    with kmap_b200.Chip(path, prefill=(mode == "prefill")) as chip:
+        if mode == "prefill":
+            toks_g = chip.infer(prompt, max_new)
+            lg_last = chip.final_logits()
+            assert toks_g.tolist() == toks_o.tolist()
+            np.testing.assert_allclose(lg_last, lg_o[len(prompt) + max_new - 1], rtol=RTOL,
+                                       atol=ATOL)
+            return
+        toks_g, lg_g = chip.infer(prompt, max_new, logits=True)
+        assert chip.stats()["step_kernel"] == 1
+    assert toks_g.tolist() == toks_o.tolist()
+    np.testing.assert_allclose(lg_g, lg_o, rtol=RTOL, atol=ATOL)
