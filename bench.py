@@ -53,9 +53,9 @@ from kmap_b200 import chipgen  # noqa: E402
 PROMPT, GEN = 32, 128
 INDEX_BYTES_PER_TOKEN = 2068840448
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_decode_step launch:
-# 311.3 MB measured on the 2-layer TinyLlama-width chip (307.2 MB of index
-# stream, ratio 1.0132), scaled to the 22-layer index stream
-STEP_TRAFFIC_BYTES = 2096203116
+# 311.1 MB measured on the 2-layer TinyLlama-width chip (307.2 MB of index
+# stream, ratio 1.0126), scaled to the 22-layer index stream
+STEP_TRAFFIC_BYTES = 2094968839
 CHIP_CACHE = os.environ.get("KLLM_CHIP_CACHE", "/tmp/kllm_chips")
 TT_SHAPES = [(2048, 2048, 4096), (2048, 5632, 5461), (5632, 2048, 5461), (2048, 32000, 5461)]
 
