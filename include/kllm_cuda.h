@@ -219,6 +219,25 @@ int kllm_chip_info(kllm_chip *chip, int *info);
 int kllm_chip_infer(kllm_chip *chip, const int *prompt, int prompt_len, int max_new,
                     int eos_token_id, int *out_tokens, int *out_len);
 
+/* Batched greedy decode of nseq independent sequences on one GPU -- the
+ * reference has no counterpart: its processor_infer (_tape_runner.c:
+ * 1602-1763) runs one sequence; this runs that loop for all of them at
+ * once, each with its own KV cache and position.  prompts holds the
+ * sequences' token IDs back to back (prompt_lens[i] each); out receives
+ * nseq x max_new tokens (row i: sequence i's greedy tokens, computed for all
+ * max_new steps), out_lens[i] the number before sequence i's first `eos`
+ * (the reference would stop there; pass -1 for none).  Prompts go through
+ * the batched prompt pass, then each step is one TT-GEMM per projection
+ * over the nseq rows, each row bit-identical to the TT-GEMV (with
+ * KLLM_BATCH_TC=1: the tensor-core GEMM, a tolerance result).  The context
+ * must not be column-sharded.  Returns 0 or non-zero (kllm_last_error);
+ * kllm_get_infer_stats gives the prompt and decode device times. */
+int kllm_infer_batch(TapeCtx *ctx, const int *prompts, const int *prompt_lens, int nseq,
+                     int max_new, int eos, int *out, int *out_lens);
+/* The same on a loaded chip (prepares its fused plan first). */
+int kllm_chip_infer_batch(kllm_chip *chip, const int *prompts, const int *prompt_lens, int nseq,
+                          int max_new, int eos, int *out, int *out_lens);
+
 /* kllm_plan_prepare with the chip's tables, for its max_seq_len. */
 int kllm_chip_plan_prepare(kllm_chip *chip);
 

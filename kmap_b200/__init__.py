@@ -60,6 +60,10 @@ _SIGS = {
     "kllm_chip_infer_bytes": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_int,
                                          C.c_void_p, C.c_void_p, _fp(C.c_int)]),
     "kllm_chip_encode": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_int, _fp(C.c_int32)]),
+    "kllm_chip_infer_batch": (C.c_int, [C.c_void_p, _fp(C.c_int), _fp(C.c_int), C.c_int, C.c_int,
+                                         C.c_int, _fp(C.c_int), _fp(C.c_int)]),
+    "kllm_infer_batch": (C.c_int, [C.c_void_p, _fp(C.c_int), _fp(C.c_int), C.c_int, C.c_int,
+                                    C.c_int, _fp(C.c_int), _fp(C.c_int)]),
     "kllm_chip_decode": (C.c_int, [C.c_void_p, _fp(C.c_int32), C.c_int, C.c_int, C.c_int,
                                     C.c_char_p]),
     "kllm_plan_match": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -318,6 +322,20 @@ class Chip:
         check(rc, "processor_infer")
         toks = out[:n.value].copy()
         return (toks, lg) if logits else toks
+
+    def infer_batch(self, prompts, max_new: int, eos: int = -1):
+        """Greedy generation for several sequences at once
+        (kllm_chip_infer_batch): returns one token array per sequence, each
+        cut before its first `eos`."""
+        lens = np.array([len(p) for p in prompts], np.int32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int32) for p in prompts]),
+                                    np.int32)
+        out = np.zeros((len(prompts), max_new), np.int32)
+        n = np.zeros(len(prompts), np.int32)
+        self.set_opts()
+        check(lib().kllm_chip_infer_batch(self.h, _iptr(flat), _iptr(lens), len(prompts), max_new,
+                                          eos, _iptr(out), _iptr(n)), "kllm_chip_infer_batch")
+        return [out[i, :n[i]].copy() for i in range(len(prompts))]
 
     def infer_bytes(self, text: bytes, max_new: int, max_seq: int = 0, stop_after: int = -1):
         """Bytes in, streamed bytes out (processor_infer_bytes)."""

@@ -341,6 +341,22 @@ int kllm_chip_infer(kllm_chip *c, const int *prompt, int prompt_len, int max_new
                            c->layers, c->n_kv, prompt, prompt_len, max_new, eos, out, out_len);
 }
 
+int kllm_chip_infer_batch(kllm_chip *c, const int *prompts, const int *prompt_lens, int nseq,
+                          int max_new, int eos, int *out, int *out_lens) {
+    if (!c || !prompt_lens || nseq < 1) {
+        set_error("kllm_chip_infer_batch: bad argument");
+        return -1;
+    }
+    for (int i = 0; i < nseq; i++)
+        if (prompt_lens[i] + std::max(max_new, 0) > c->max_seq) {
+            set_error("kllm_chip_infer_batch: sequence %d: %d positions exceed the chip's RoPE "
+                      "table of %d", i, prompt_lens[i] + max_new, c->max_seq);
+            return -1;
+        }
+    if (kllm_chip_plan_prepare(c) != 0) return -1;
+    return kllm_infer_batch(c->ctx, prompts, prompt_lens, nseq, max_new, eos, out, out_lens);
+}
+
 int kllm_chip_plan_prepare(kllm_chip *c) {
     if (!c) {
         set_error("kllm_chip_plan_prepare: NULL chip");

@@ -227,6 +227,30 @@ struct ByteSink : TokenSink {
 };
 }  // namespace
 
+extern "C" int kllm_infer_batch(TapeCtx *ctx, const int *prompts, const int *prompt_lens,
+                                int nseq, int max_new, int eos, int *out, int *out_lens) {
+    if (!ctx || !prompts || !prompt_lens || !out || !out_lens || nseq < 1 || max_new < 1) {
+        set_error("kllm_infer_batch: bad argument");
+        return -1;
+    }
+    CtxImpl *c = impl(ctx);
+    if (!select_device(c)) return -1;
+    auto t0 = std::chrono::steady_clock::now();
+    memset(&c->stats, 0, sizeof c->stats);
+    const long long l0 = g_launches;
+    double pre = 0, dec = 0;
+    const bool ok = plan_infer_batch(c, prompts, prompt_lens, nseq, max_new, eos, out, out_lens,
+                                     &pre, &dec);
+    c->stats.fused = 1;
+    c->stats.steps = max_new;
+    c->stats.prefill_ms = pre;
+    c->stats.decode_ms = dec;
+    c->stats.launches = g_launches - l0;
+    c->stats.total_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ok ? 0 : -1;
+}
+
 extern "C" int kllm_plan_prepare(TapeCtx *ctx, const float *embed_table, int vocab_size,
                                  int hidden_dim, const float *rope_cos, const float *rope_sin,
                                  int head_dim, int token_embed_slot, int rope_cos_slot,

@@ -39,6 +39,7 @@
 #include "sm100.cuh"
 #include "tt_fused.cuh"
 #include "persist.cuh"
+#include "batch.cuh"
 #include "prefill.cuh"
 
 namespace kllm {
@@ -519,6 +520,10 @@ struct DecodePlan {
     // ([N][K], 4 per layer: qkv, o, gate_up, down), built at the first pass
     std::vector<void *> pf_wt;
     int pf_terms = 0;    // bf16 terms of x (0: the exact FP32 TT-GEMM)
+    // batched decode of several sequences: caches and rows, grown as needed
+    float *bd_arena = nullptr;
+    size_t bd_cap = 0;   // floats
+    void *bd_lm_wt = nullptr;   // lm_head as bf16 Wt (tensor-core batches)
 #ifdef KLLM_DS_PROFILE
     unsigned long long *prof = nullptr;   // step timestamps (profiling build)
     size_t prof_n = 0;
@@ -531,7 +536,8 @@ static void free_plan(DecodePlan *p) {
     if (p->graph) cudaGraphDestroy(p->graph);
     void *bufs[] = {p->embed, p->rcos, p->rsin, p->h, p->qkv, p->ctx, p->act, p->logits,
                     p->part, p->counters, p->kc, p->vc, p->cand_v, p->cand_i,
-                    p->st, p->prompt, p->gen, p->status, p->hist, p->pf_arena
+                    p->st, p->prompt, p->gen, p->status, p->hist, p->pf_arena, p->bd_arena,
+                    p->bd_lm_wt
 #ifdef KLLM_DS_PROFILE
                     , p->prof
 #endif
@@ -1272,7 +1278,8 @@ static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
 // prompt's last position then runs as a regular decode step, which picks
 // the first token.  Its activations live in one arena of the plan, grown
 // (once) to the longest prompt seen and freed with the plan.
-static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
+static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, const int *prompt_dev, float *kc_base,
+                         float *vc_base, cudaStream_t s) {
     const TemplateInfo &t = p->ti;
     const TapeCtx *ctx = &c->base;
     const int H = t.H, hd = t.hd, nh = t.nh, nkv = t.nkv, F = t.F, L = t.L;
@@ -1360,13 +1367,13 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
                                             (int)att_smem));
     }
     if (ok) {
-        k_pf_embed<<<R, PF_THREADS, 0, s>>>(p->embed, p->prompt, H, hA);
+        k_pf_embed<<<R, PF_THREADS, 0, s>>>(p->embed, prompt_dev, H, hA);
         g_launches++;
     }
     for (int l = 0; ok && l < L; l++) {
         const LayerSlots &ls = t.layers[l];
         cur_layer = l;
-        float *kc = p->kc + (size_t)l * nkv * mp * hd, *vc = p->vc + (size_t)l * nkv * mp * hd;
+        float *kc = kc_base + (size_t)l * nkv * mp * hd, *vc = vc_base + (size_t)l * nkv * mp * hd;
         k_pf_rmsnorm<<<R, PF_THREADS, 0, s>>>(hA, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
         ok = gemm(ls.qkv, xn, big);
         if (!ok) break;
@@ -1396,6 +1403,190 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, cudaStream_t s) {
         ok = KLLM_CUDA(cudaGetLastError());
     }
     return ok && KLLM_CUDA(cudaGetLastError());
+}
+
+// Batched greedy decode of nseq independent sequences (no counterpart in the
+// reference: its processor_infer, _tape_runner.c:1602-1763, runs one
+// sequence; this is that loop for many sequences at once).  Each prompt but
+// its last position goes through the batched prompt pass into the
+// sequence's own KV cache; then every step feeds one token per sequence:
+// embedding rows, per layer row RMSNorm, the QKV / O / gate_up / down
+// projections as one TT-GEMM over the nseq rows (each row bit-identical to
+// the TT-GEMV, or on the tensor cores with KLLM_BATCH_TC=1), RoPE and the
+// append at each row's own position, attention over each row's own cache,
+// residual adds and SwiGLU; final norm, lm_head, the first-maximum pick per
+// row.  Sequences run the full max_new steps; out_lens cut each at its
+// first EOS (the reference stops there and emits nothing after it).
+bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq, int max_new,
+                      int eos, int *out, int *out_lens, double *prefill_ms, double *decode_ms) {
+    DecodePlan *p = c->plan;
+    if (!p || !p->persist) {
+        set_error("batched decode: no fused decode plan");
+        return false;
+    }
+    if (p->world != 1) {
+        set_error("batched decode runs on one GPU (the context is column-sharded)");
+        return false;
+    }
+    const TemplateInfo &t = p->ti;
+    const TapeCtx *ctx = &c->base;
+    const int H = t.H, hd = t.hd, nh = t.nh, nkv = t.nkv, F = t.F, L = t.L, V = t.V;
+    const int qd = nh * hd, kvd = nkv * hd, nq = qd + 2 * kvd, mp = p->max_pos;
+    if (nseq < 1 || max_new < 1 || PF_THREADS % hd) {
+        set_error("batched decode: %d sequences, %d new tokens, head dim %d", nseq, max_new, hd);
+        return false;
+    }
+    size_t total = 0;
+    for (int i = 0; i < nseq; i++) {
+        if (lens[i] < 1 || lens[i] + max_new > mp) {
+            set_error("batched decode: sequence %d has %d prompt tokens (+%d) for %d positions", i,
+                      lens[i], max_new, mp);
+            return false;
+        }
+        for (int j = 0; j < lens[i]; j++)
+            if (prompts[total + j] < 0 || prompts[total + j] >= V) {
+                set_error("batched decode: prompt token %d of sequence %d outside the vocabulary",
+                          j, i);
+                return false;
+            }
+        total += lens[i];
+    }
+    cudaStream_t s = c->stream;
+    const bool tc = env_on("KLLM_BATCH_TC", false) && p->vm == TTX_VBF16;
+    // arena (floats, each piece a multiple of 4): K and V caches of every
+    // sequence; rows h, hB, xn [nseq][H]; big [nseq][max(nq, 2F, H, V)]; qr,
+    // cx [nseq][qd]; act [nseq][F]; bf16 terms of a projection's input; ints:
+    // prompts, tokens, positions, generated tokens
+    auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
+    const size_t seq_stride = (size_t)L * nkv * mp * hd;
+    const size_t kv = up4((size_t)nseq * seq_stride);
+    const size_t rh = up4((size_t)nseq * H), rq = up4((size_t)nseq * qd), rf = up4((size_t)nseq * F);
+    const size_t wide = up4((size_t)nseq * std::max({(size_t)nq, (size_t)2 * F, (size_t)H, (size_t)V}));
+    const size_t rxs = up4(((size_t)3 * nseq * std::max({(size_t)H, (size_t)F, (size_t)qd}) + 1) / 2);
+    const size_t ints = up4(total + 2 * (size_t)nseq + (size_t)nseq * max_new);
+    const size_t need = 2 * kv + 3 * rh + wide + 2 * rq + rf + rxs + ints;
+    if (p->bd_cap < need) {
+        if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
+        if (p->bd_arena) cudaFree(p->bd_arena);
+        p->bd_arena = nullptr;
+        p->bd_cap = 0;
+        if (!dalloc(&p->bd_arena, need)) return false;
+        p->bd_cap = need;
+    }
+    float *kcs = p->bd_arena, *vcs = kcs + kv, *h = vcs + kv, *hB = h + rh, *xn = hB + rh,
+          *big = xn + rh, *qr = big + wide, *cx = qr + rq, *act = cx + rq, *xs = act + rf;
+    int *d_prompts = reinterpret_cast<int *>(xs + rxs), *d_tok = d_prompts + total,
+        *d_pos = d_tok + nseq, *d_gen = d_pos + nseq;
+    std::vector<int> tok0(nseq), pos0(nseq);
+    {
+        size_t off = 0;
+        for (int i = 0; i < nseq; i++) {
+            tok0[i] = prompts[off + lens[i] - 1];
+            pos0[i] = lens[i] - 1;
+            off += lens[i];
+        }
+    }
+    if (!KLLM_CUDA(cudaMemcpyAsync(d_prompts, prompts, total * 4, cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemcpyAsync(d_tok, tok0.data(), nseq * 4, cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemcpyAsync(d_pos, pos0.data(), nseq * 4, cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemsetAsync(p->status, 0, 4, s)))
+        return false;
+    // the lm_head as bf16 Wt for the tensor-core form (built once)
+    const Slot &lms = ctx->slots[t.lm];
+    const bool lm_tc = tc && pf_gemm_applies(lms.tt_K, lms.tt_N);
+    if (lm_tc && !p->bd_lm_wt) {
+        if (!KLLM_CUDA(cudaMalloc(&p->bd_lm_wt, (size_t)lms.tt_K * lms.tt_N * 2)) ||
+            !pf_build_wt(s, c->ds[t.lm].d_idx, c->ds[t.lm].d_cb, lms.tt_K, lms.tt_N, p->bd_lm_wt))
+            return false;
+    }
+    if (!KLLM_CUDA(cudaEventRecord(p->ev0, s))) return false;
+    // prompt passes, one sequence after another, into the sequences' caches
+    {
+        size_t off = 0;
+        for (int i = 0; i < nseq; i++) {
+            if (lens[i] >= 2 && !plan_prefill(c, p, lens[i] - 1, d_prompts + off,
+                                              kcs + (size_t)i * seq_stride,
+                                              vcs + (size_t)i * seq_stride, s))
+                return false;
+            off += lens[i];
+        }
+    }
+    if (!KLLM_CUDA(cudaEventRecord(p->ev1, s))) return false;
+    const bool layer_tc = tc && p->pf_terms > 0;   // the prompt pass built the layers' Wt
+    auto gemm = [&](int slot, int layer, int which, const float *x, float *y) {
+        const Slot &sl = ctx->slots[slot];
+        const DevSlot &w = c->ds[slot];
+        const void *wt = which < 4 ? (layer_tc ? p->pf_wt[(size_t)4 * layer + which] : nullptr)
+                                   : (lm_tc ? p->bd_lm_wt : nullptr);
+        if (wt)
+            return pf_split(s, x, (long long)nseq * sl.tt_K, 3, xs) &&
+                   pf_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, y, p->status);
+        return kllm_tt_gemm(x, nseq, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
+    };
+    const int ew_blocks = 148 * 8;
+    const size_t att_smem = (size_t)std::max(mp, PF_THREADS) * 4;
+    if (att_smem > 48 * 1024 &&
+        !KLLM_CUDA(cudaFuncSetAttribute(k_bd_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)att_smem)))
+        return false;
+    bool ok = true;
+    for (int step = 0; ok && step < max_new; step++) {
+        k_pf_embed<<<nseq, PF_THREADS, 0, s>>>(p->embed, d_tok, H, h);
+        g_launches++;
+        for (int l = 0; ok && l < L; l++) {
+            const LayerSlots &ls = t.layers[l];
+            float *kc = kcs + (size_t)l * nkv * mp * hd, *vc = vcs + (size_t)l * nkv * mp * hd;
+            k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
+            ok = gemm(ls.qkv, l, 0, xn, big);
+            if (!ok) break;
+            k_bd_rope_kv<<<nseq, PF_THREADS, 0, s>>>(big, d_pos, nq, nh, nkv, hd, p->rcos, p->rsin,
+                                                     mp, seq_stride, qr, kc, vc);
+            k_bd_attention<<<dim3(nseq, nh), PF_THREADS, att_smem, s>>>(
+                qr, kc, vc, d_pos, nh, t.groups, hd, mp, seq_stride, p->scale, cx);
+            ok = gemm(ls.o, l, 1, cx, big);
+            if (!ok) break;
+            k_pf_add<<<ew_blocks, 256, 0, s>>>(h, big, (long long)nseq * H, hB);
+            k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], H,
+                                                    xn);
+            ok = gemm(ls.gu, l, 2, xn, big);
+            if (!ok) break;
+            k_pf_swiglu<<<ew_blocks, 256, 0, s>>>(big, F, (long long)nseq * F, act);
+            ok = gemm(ls.dn, l, 3, act, big);
+            if (!ok) break;
+            k_pf_add<<<ew_blocks, 256, 0, s>>>(hB, big, (long long)nseq * H, h);
+            g_launches += 7;
+        }
+        if (!ok) break;
+        k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm.back(), p->f_eps, H, xn);
+        ok = gemm(t.lm, 0, 4, xn, big);
+        if (!ok) break;
+        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(big, V, step, max_new, d_tok, d_pos, d_gen);
+        g_launches += 3;
+        ok = KLLM_CUDA(cudaGetLastError());
+    }
+    if (!ok || !KLLM_CUDA(cudaEventRecord(p->ev2, s))) return false;
+    std::vector<int> gen((size_t)nseq * max_new);
+    int status = 0;
+    if (!KLLM_CUDA(cudaMemcpyAsync(gen.data(), d_gen, gen.size() * 4, cudaMemcpyDeviceToHost, s)) ||
+        !KLLM_CUDA(cudaMemcpyAsync(&status, p->status, 4, cudaMemcpyDeviceToHost, s)) ||
+        !KLLM_CUDA(cudaStreamSynchronize(s)))
+        return false;
+    if (status) {
+        set_error("batched decode kernels reported status 0x%x", status);
+        return false;
+    }
+    for (int i = 0; i < nseq; i++) {
+        int n = 0;
+        while (n < max_new && gen[(size_t)i * max_new + n] != eos) n++;
+        memcpy(out + (size_t)i * max_new, gen.data() + (size_t)i * max_new, (size_t)max_new * 4);
+        out_lens[i] = n;
+    }
+    float pre = 0.f, dec = 0.f;
+    cudaEventElapsedTime(&pre, p->ev0, p->ev1);
+    cudaEventElapsedTime(&dec, p->ev1, p->ev2);
+    if (prefill_ms) *prefill_ms = pre;
+    if (decode_ms) *decode_ms = dec;
+    return true;
 }
 
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,
@@ -1466,7 +1657,7 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
     if (c->opts.prefill && p->persist && want_rows == 0 && prompt_len >= 2) {
         const int R = prompt_len - 1;
         StepState st1 = {R, prompt_len, 0, 0};
-        if (!plan_prefill(c, p, R, s) ||
+        if (!plan_prefill(c, p, R, p->prompt, p->kc, p->vc, s) ||
             !KLLM_CUDA(cudaMemcpyAsync(p->st, &st1, sizeof st1, cudaMemcpyHostToDevice, s)))
             return false;
         launched = R;

@@ -39,4 +39,10 @@ void plan_kind(const CtxImpl *c, int *persist, int *values);
 bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int max_pos,
                 int eos, const std::function<bool(int, int)> &emit, int *generated);
 
+// Batched greedy decode of nseq sequences (prompts concatenated, lens[i]
+// tokens each): out[i * max_new + j] is sequence i's token j, out_lens[i]
+// the count before its first EOS.  One GPU, persistent plan prepared.
+bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq, int max_new,
+                      int eos, int *out, int *out_lens, double *prefill_ms, double *decode_ms);
+
 }  // namespace kllm

@@ -138,3 +138,16 @@ def test_fused_plan_rejects_changed_tapes(built_lib, chip_dir):
         ko = [m["output_map"]["L%d/new_%s" % (l, c)] for l in range(2) for c in "kv"]
         ko[1], ko[0] = ko[0], ko[1]
         assert not chip.plan_match(kv_out=ko)[0]
+
+
+def test_infer_batch_rejects_bad_arguments(built_lib):
+    import ctypes as C
+
+    import kmap_b200
+    lib = kmap_b200.lib()
+    one = (C.c_int * 4)(1, 1, 1, 1)
+    assert lib.kllm_infer_batch(None, one, one, 1, 1, -1, one, one) == -1
+    assert b"bad argument" in lib.kllm_last_error()
+    lib.kllm_clear_error()
+    assert lib.kllm_chip_infer_batch(None, one, one, 1, 1, -1, one, one) == -1
+    lib.kllm_clear_error()
