@@ -139,7 +139,11 @@ class Clocks:
 def ttgemv_roofline(device_index):
     """Average launch time of the TT-GEMV on the config-1 shapes, timed with
     CUDA events on the launching stream; copies rotate so that every launch
-    reads its indices from HBM."""
+    reads its indices from HBM.  `us`: one launch per copy captured in a CUDA
+    graph and replayed, so the kernels run back to back (the device time of
+    a launch); `us_host_loop`: the same launches issued one by one from
+    Python through the C ABI (bounded by the host's call rate for the small
+    shapes)."""
     import torch
 
     import kmap_b200
@@ -171,9 +175,26 @@ def ttgemv_roofline(device_index):
             run(i)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / reps
+        ms_host = e0.elapsed_time(e1) / reps
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cs = torch.cuda.current_stream(dev)
+            for i in range(copies):
+                rc = lib.kllm_tt_gemv(d_x.data_ptr(), 1, d_cb.data_ptr(), C,
+                                      d_idx[i].data_ptr(), K, N, d_y.data_ptr(), cs.cuda_stream)
+                assert rc == 0, kmap_b200.last_error()
+        g.replay()
+        torch.cuda.synchronize(dev)
+        greps = max(3, -(-reps // copies))
+        e0.record(stream)
+        for _ in range(greps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / (greps * copies)
+        del g
         res.append({"K": K, "N": N, "codes": C, "us": ms * 1e3,
-                    "gbs": K * N * 2 / (ms * 1e-3) / 1e9})
+                    "gbs": K * N * 2 / (ms * 1e-3) / 1e9, "us_host_loop": ms_host * 1e3})
         del d_idx
     return res
 
@@ -780,6 +801,166 @@ def run_config3(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+C4_SEQS, C4_PROMPT, C4_GEN = 32, 1024, 128
+
+
+def c4_chip(local_rank):
+    """The Llama-3-8B-architecture chip (32 x 4096, 32 query / 8 kv heads of
+    128, SwiGLU 14336, vocab 128256, rope theta 5e5, max_seq 1152), weights
+    drawn on the GPU."""
+    import fcntl
+
+    import torch
+    spec = chipgen.ModelSpec(**{**chipgen.LLAMA3_8B.__dict__})
+    os.makedirs(CHIP_CACHE, exist_ok=True)
+    with open(os.path.join(CHIP_CACHE, ".lock"), "w") as f:
+        fcntl.flock(f, fcntl.LOCK_EX)
+        t = time.time()
+        path = chipgen.ensure_chip(CHIP_CACHE, spec, device=torch.device("cuda", local_rank))
+        log("8B chip ready in %.1fs: %s" % (time.time() - t, path))
+    return path, spec
+
+
+def run_config4(args, rank, world, local_rank):
+    """Config 4: greedy decode of 32 concurrent sequences (1024-token
+    uniform-random prompts, 128 generated tokens each) on the
+    Llama-3-8B-architecture chip.  Each sequence's prompt goes through the
+    batched prompt pass into its own KV cache; every decode step then runs
+    each projection once over the 32 rows (the skinny tensor-core GEMM,
+    weight bytes read once per step), attention per sequence.  With N GPUs
+    the sequences are divided among the ranks (independent sequences: no
+    data-path collective), each rank with the whole chip.  value = generated
+    tokens per second of decode device time, all sequences; e2e = the same
+    tokens per second of wall time of the whole call (prompt upload, prompt
+    passes, decode, token read-back).  Parity: a 4-sequence batch of short
+    prompts against each sequence's single-sequence decode (the exact
+    persistent step, bit-identical to the reference's MATMUL_TT) and one
+    sequence against the compiled reference."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    import torch
+    torch.cuda.set_device(local_rank)
+    kmap_b200.lib().kllm_set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                device_id=torch.device("cuda", local_rank))
+    path, spec = c4_chip(local_rank)
+    if dist:
+        dist.barrier()
+    t_open = time.time()
+    chip = kmap_b200.Chip(path)
+    t_open = time.time() - t_open
+    V = chip.info["vocab_size"]
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(3, V, C4_PROMPT).astype(np.int32) for _ in range(C4_SEQS)]
+    mine = prompts[rank::world]
+    # parity first: short prompts, batch vs one sequence at a time
+    srng = np.random.default_rng(12)
+    short = [srng.integers(3, V, 16 + i).astype(np.int32) for i in range(4)]
+    t0 = time.time()
+    b_short = chip.infer_batch(short, 8)
+    t_first = time.time() - t0
+    singles = [chip.infer(p, 8) for p in short]
+    for _ in range(args.warmup):
+        chip.infer_batch(mine, C4_GEN)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    pre_ms, dec_ms, wall, gen = 0.0, 0.0, 0.0, 0
+    with Clocks(local_rank) as clk:
+        for _ in range(args.steps):
+            t = time.time()
+            outs = chip.infer_batch(mine, C4_GEN)
+            wall += time.time() - t
+            st = chip.stats()
+            pre_ms += st["prefill_ms"]
+            dec_ms += st["decode_ms"]
+            gen += sum(len(o) for o in outs)
+    launches = chip.stats().get("launches")
+    barrier()
+    tt = torch.tensor([pre_ms, dec_ms, wall, gen], dtype=torch.float64, device="cuda")
+    if dist:
+        mx = tt[:3].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        g = tt[3:].clone()
+        dist.all_reduce(g, op=dist.ReduceOp.SUM)
+        tt = torch.cat([mx, g])
+    pre_ms, dec_ms, wall, gen = tt.tolist()
+    chip.close()
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    H, F, L, Vv = spec.hidden_size, spec.intermediate_size, spec.num_layers, spec.vocab_size
+    hd = H // spec.num_attention_heads
+    kvd = spec.num_key_value_heads * hd
+    w_bytes = 2 * (L * (H * (H + 2 * kvd) + H * H + H * 2 * F + F * H) + H * Vv)
+    # k and v rows read per step, summed over the steps (n = pos + 1 per row)
+    kv_rows = C4_SEQS * sum(C4_PROMPT + i for i in range(C4_GEN))
+    kv_bytes = kv_rows * L * kvd * 4 * 2
+    step_bytes = w_bytes + kv_bytes / C4_GEN
+    step_us = dec_ms * 1e3 / (args.steps * C4_GEN)
+    gbs = step_bytes / (step_us * 1e-6) / 1e9
+    hbm = peaks().get("hbm_gbs")
+    out = {"metric": "batched decode tok/s (generated tokens per second of decode device "
+                     "time, all sequences)",
+           "value": gen / (dec_ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": dec_ms / args.steps, "higher_is_better": True,
+           "scaling": "strong" if world > 1 else "weak", "dtype": "bf16 tensor-core GEMM, f32",
+           "data": "synthetic",
+           "config": {"workload": "Llama-3-8B-arch TT chip (32x4096, 32 query / 8 kv heads of "
+                      "128, SwiGLU 14336, vocab 128256, rope theta 5e5, bf16-rounded N(0,0.02) "
+                      "drawn on the GPU), 32 sequences x (1024-token prompt + 128 greedy "
+                      "tokens)",
+                      "parallelism": ("sequences divided over %d GPUs" % world if world > 1
+                                      else "single GPU"),
+                      "l2": "weights 15 GB and caches 9 GB per step exceed L2"},
+           "e2e": {"value": gen / wall, "unit": "tok/s",
+                   "h2d_bytes_per_step": 4 * C4_SEQS * C4_PROMPT,
+                   "d2h_bytes_per_step": 4 * C4_SEQS * C4_GEN,
+                   "note": "wall time of kllm_chip_infer_batch: prompt passes included"},
+           "prefill": {"tok_s": args.steps * C4_SEQS * (C4_PROMPT - 1) / (pre_ms / 1e3),
+                       "ms_per_batch": pre_ms / args.steps},
+           "roofline": {"bound": "hbm", "kernel": "one decode step of 32 sequences "
+                        "(graph: skinny tcgen05 GEMMs, grouped attention, row kernels)",
+                        "launch_us": step_us,
+                        "algorithmic_bytes_per_launch": step_bytes,
+                        "weight_bytes": w_bytes, "kv_bytes_mean": kv_bytes / C4_GEN,
+                        "achieved": gbs, "peak": hbm * world if hbm else None, "unit": "GB/s",
+                        "frac": gbs / (hbm * world) if hbm else None},
+           "gpu_launches": launches,
+           "load": {"chip_open_s": t_open, "first_call_s": t_first},
+           "parity": {"batch_vs_single_sequence_tokens_equal":
+                      all(a.tolist() == b.tolist() for a, b in zip(b_short, singles)),
+                      "sequences": "4 prompts of 16..19 tokens + 8 greedy tokens"},
+           "clocks": clk.summary()}
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import harness
+    if harness.have_ref() and not args.no_cpu_baseline:
+        ref = harness.Ref()
+        h, info = ref.chip(path)
+        t = time.time()
+        rt = ref.infer(h, short[0][:8], 4)
+        dt = time.time() - t
+        ref.L.refh_chip_destroy(h)
+        with kmap_b200.Chip(path) as c2:
+            ours = c2.infer_batch([short[0][:8], short[1][:8]], 4)[0]
+        out["parity"]["reference"] = ("compiled reference runtime, same chip, 8-token prompt "
+                                      "+ 4 greedy tokens (%.1f s on the host)" % dt)
+        out["parity"]["reference_tokens_equal"] = rt.tolist() == ours.tolist()
+    print(json.dumps(out), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -795,9 +976,10 @@ def main():
     ap.add_argument("--no-fast", action="store_true",
                     help="leave the fast-order comparison out of the JSON line")
     ap.add_argument("--cpu-sample", metavar="OUT", help=argparse.SUPPRESS)
-    ap.add_argument("--model", default="tinyllama-1.1b", choices=["tinyllama-1.1b", "llama2-7b"],
+    ap.add_argument("--model", default="tinyllama-1.1b", choices=["tinyllama-1.1b", "llama2-7b", "llama3-8b-batch"],
                     help="llama2-7b: the 7B-architecture decode workload (4096-token prompt, "
-                         "256 tokens) as its own JSON line")
+                         "256 tokens) as its own JSON line; llama3-8b-batch: 32 sequences "
+                         "of 1024 + 128 tokens on the 8B-architecture chip")
     ap.add_argument("--order", default="exact", choices=["exact", "fast"],
                     help="TT-GEMV summation order of the decode step: the reference's "
                          "chunked order (bit-identical MATMUL_TT) or the finer split")
@@ -835,6 +1017,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.model == "llama2-7b":
         run_config3(args, rank, world, local_rank)
+    elif args.model == "llama3-8b-batch":
+        run_config4(args, rank, world, local_rank)
     elif args.impl == "reference":
         run_reference_arm(args, rank, world)
     else:

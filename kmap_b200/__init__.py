@@ -323,7 +323,7 @@ class Chip:
         toks = out[:n.value].copy()
         return (toks, lg) if logits else toks
 
-    def infer_batch(self, prompts, max_new: int, eos: int = -1):
+    def infer_batch(self, prompts, max_new: int, eos: int = -1, use_graphs: bool = True):
         """Greedy generation for several sequences at once
         (kllm_chip_infer_batch): returns one token array per sequence, each
         cut before its first `eos`."""
@@ -332,7 +332,7 @@ class Chip:
                                     np.int32)
         out = np.zeros((len(prompts), max_new), np.int32)
         n = np.zeros(len(prompts), np.int32)
-        self.set_opts()
+        self.set_opts(use_graphs=use_graphs)
         check(lib().kllm_chip_infer_batch(self.h, _iptr(flat), _iptr(lens), len(prompts), max_new,
                                           eos, _iptr(out), _iptr(n)), "kllm_chip_infer_batch")
         return [out[i, :n[i]].copy() for i in range(len(prompts))]

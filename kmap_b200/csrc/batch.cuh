@@ -42,60 +42,148 @@ __global__ void k_bd_rope_kv(const float *__restrict__ qkv, const int *__restric
     }
 }
 
-// Attention of row r (position pos[r]), head h, over positions 0..pos[r]
-// of sequence r's cache: scores q.k * scale, max-subtracted exp in double,
-// sum, divide, P.V.  (grid: nseq x nh blocks, PF_THREADS threads, dynamic
-// shared memory: max(max_pos, PF_THREADS) floats; hd divides PF_THREADS)
-__global__ void k_bd_attention(const float *__restrict__ q, const float *__restrict__ kc,
-                               const float *__restrict__ vc, const int *__restrict__ pos, int nh,
-                               int groups, int hd, int max_pos, size_t seq_stride, float scale,
-                               float *__restrict__ ctx) {
-    extern __shared__ float sc[];
-    __shared__ float red[PF_THREADS / 32];
-    const int r = blockIdx.x, h = blockIdx.y, g = h / groups, n = pos[r] + 1;
-    const int qd = nh * hd;
-    const float *qr = q + (size_t)r * qd + h * hd;
-    const float *kg = kc + (size_t)r * seq_stride + (size_t)g * max_pos * hd;
-    const float *vg = vc + (size_t)r * seq_stride + (size_t)g * max_pos * hd;
-    float m = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += PF_THREADS) {
-        float dot = 0.f;
-        for (int d = 0; d < hd; d++) dot = __fadd_rn(dot, __fmul_rn(qr[d], kg[(size_t)j * hd + d]));
-        const float s = __fmul_rn(dot, scale);
-        sc[j] = s;
-        m = fmaxf(m, s);
+// Attention of row r for the `groups` query heads of kv head g at once
+// (each cached k / v row read once): grid nseq x nkv, BD_ATT_THREADS
+// threads.  Scores: warp w takes positions w, w + 8, ...; lane i holds
+// dims [VEC i, VEC i + VEC) of the row; q.k is the lane's serial sum over
+// its dims, then the xor-shuffle tree over the lanes, times the scale.
+// Softmax of query head j by warp j: max, exp in double of the difference,
+// the lanes' serial sums then the tree, division.  P.V: warp w sums its
+// positions serially per dim, the 8 warps' sums added in warp order.
+// Dynamic shared memory: bd_att_smem(groups, HD, max_pos) bytes.
+constexpr int BD_ATT_THREADS = 256;
+
+__host__ __device__ inline size_t bd_att_smem(int groups, int hd, int max_pos) {
+    return ((size_t)groups * max_pos + (size_t)groups * hd +
+            (size_t)(BD_ATT_THREADS / 32) * groups * hd) * 4;
+}
+
+template <int VEC>
+__device__ __forceinline__ void bd_load(const float *p, float (&v)[VEC]) {
+    if constexpr (VEC == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(p);
+        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else if constexpr (VEC == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(p);
+        v[0] = t.x, v[1] = t.y;
+    } else {
+        v[0] = *p;
     }
-    const float mx = pf_block_max(m, red);
-    float sum = 0.f;
-    for (int j = threadIdx.x; j < n; j += PF_THREADS) {
-        const float e = (float)exp((double)__fsub_rn(sc[j], mx));
-        sc[j] = e;
-        sum = __fadd_rn(sum, e);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(BD_ATT_THREADS)
+k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
+                const float *__restrict__ vc, const int *__restrict__ pos, int nh, int groups,
+                int max_pos, size_t seq_stride, float scale, float *__restrict__ ctx) {
+    constexpr int VEC = HD / 32, NW = BD_ATT_THREADS / 32, U = 4, GB = 8;
+    extern __shared__ float bsm[];
+    const int r = blockIdx.x, g = blockIdx.y, n = pos[r] + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float *sc = bsm;                                   // [groups][max_pos]
+    float *qs = sc + (size_t)groups * max_pos;         // [groups][HD]
+    float *pv = qs + groups * HD;                      // [NW][groups][HD]
+    const int qd = nh * HD;
+    const float *qrow = q + (size_t)r * qd + (size_t)g * groups * HD;
+    const float *kg = kc + (size_t)r * seq_stride + (size_t)g * max_pos * HD + VEC * lane;
+    const float *vg = vc + (size_t)r * seq_stride + (size_t)g * max_pos * HD + VEC * lane;
+    for (int i = threadIdx.x; i < groups * HD; i += BD_ATT_THREADS) qs[i] = qrow[i];
+    __syncthreads();
+    // scores: U positions of this warp in flight at a time
+    for (int j0 = warp; j0 < n; j0 += U * NW) {
+        float kv[U][VEC];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = j0 + u * NW;
+            if (j < n)
+                bd_load<VEC>(kg + (size_t)j * HD, kv[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = j0 + u * NW;
+            if (j >= n) break;
+            for (int hq = 0; hq < groups; hq++) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < VEC; e++)
+                    d = __fadd_rn(d, __fmul_rn(qs[hq * HD + VEC * lane + e], kv[u][e]));
+#pragma unroll
+                for (int o = 16; o; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+                if (lane == 0) sc[(size_t)hq * max_pos + j] = __fmul_rn(d, scale);
+            }
+        }
     }
-    const float tot = pf_block_sum(sum, red);
-    for (int j = threadIdx.x; j < n; j += PF_THREADS) sc[j] = __fdiv_rn(sc[j], tot);
     __syncthreads();
-    // P.V: PF_THREADS / hd position groups per dim, summed in group order
-    const int per = PF_THREADS / hd;   // hd divides PF_THREADS (32, 64, 128)
-    const int d = threadIdx.x % hd, grp = threadIdx.x / hd;
-    float acc = 0.f;
-    for (int j = grp; j < n; j += per) acc = __fadd_rn(acc, __fmul_rn(sc[j], vg[(size_t)j * hd + d]));
+    for (int hq = warp; hq < groups; hq += NW) {
+        float *row = sc + (size_t)hq * max_pos;
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sum = 0.f;
+        for (int j = lane; j < n; j += 32) {
+            const float e = (float)exp((double)__fsub_rn(row[j], m));
+            row[j] = e;
+            sum = __fadd_rn(sum, e);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        for (int j = lane; j < n; j += 32) row[j] = __fdiv_rn(row[j], sum);
+    }
     __syncthreads();
-    sc[threadIdx.x] = acc;   // sc is free again (n >= 1 entries were read above)
+    // P.V: each v row read once per block of GB query heads
+    for (int h0 = 0; h0 < groups; h0 += GB) {
+        float acc[GB][VEC];
+#pragma unroll
+        for (int hh = 0; hh < GB; hh++)
+#pragma unroll
+            for (int e = 0; e < VEC; e++) acc[hh][e] = 0.f;
+        for (int j0 = warp; j0 < n; j0 += U * NW) {
+            float vv[U][VEC];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int j = j0 + u * NW;
+                if (j < n)
+                    bd_load<VEC>(vg + (size_t)j * HD, vv[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int j = j0 + u * NW;
+                if (j >= n) break;
+#pragma unroll
+                for (int hh = 0; hh < GB; hh++) {
+                    if (h0 + hh >= groups) break;
+                    const float pj = sc[(size_t)(h0 + hh) * max_pos + j];
+#pragma unroll
+                    for (int e = 0; e < VEC; e++)
+                        acc[hh][e] = __fadd_rn(acc[hh][e], __fmul_rn(pj, vv[u][e]));
+                }
+            }
+        }
+#pragma unroll
+        for (int hh = 0; hh < GB; hh++) {
+            if (h0 + hh >= groups) break;
+#pragma unroll
+            for (int e = 0; e < VEC; e++)
+                pv[((size_t)warp * groups + h0 + hh) * HD + VEC * lane + e] = acc[hh][e];
+        }
+    }
     __syncthreads();
-    if (grp == 0) {
-        float o = sc[d];
-        for (int i = 1; i < per; i++) o = __fadd_rn(o, sc[i * hd + d]);
-        ctx[(size_t)r * qd + h * hd + d] = o;
+    float *out = ctx + (size_t)r * qd + (size_t)g * groups * HD;
+    for (int i = threadIdx.x; i < groups * HD; i += BD_ATT_THREADS) {
+        float o = pv[i];
+        for (int w = 1; w < NW; w++) o = __fadd_rn(o, pv[(size_t)w * groups * HD + i]);
+        out[i] = o;
     }
 }
 
 // Greedy pick of row r (the reference's: best = logits[0], then strict >
 // over the rest in index order), written as the row's next token and as
-// generated token `step`; the row's position advances.  (grid: nseq
-// blocks, PF_THREADS threads)
-__global__ void k_bd_argmax(const float *__restrict__ logits, int V, int step, int max_new,
-                            int *__restrict__ tok, int *__restrict__ pos, int *__restrict__ gen) {
+// its generated token pos[r] - start[r]; the row's position advances.
+// (grid: nseq blocks, PF_THREADS threads)
+__global__ void k_bd_argmax(const float *__restrict__ logits, int V, const int *__restrict__ start,
+                            int max_new, int *__restrict__ tok, int *__restrict__ pos,
+                            int *__restrict__ gen) {
     __shared__ float bv[PF_THREADS];
     __shared__ int bi[PF_THREADS];
     const int r = blockIdx.x;
@@ -123,7 +211,8 @@ __global__ void k_bd_argmax(const float *__restrict__ logits, int V, int step, i
                 }
         }
         tok[r] = k;
-        gen[(size_t)r * max_new + step] = k;
+        const int step = pos[r] - start[r];
+        if (step >= 0 && step < max_new) gen[(size_t)r * max_new + step] = k;
         pos[r] = pos[r] + 1;
     }
 }

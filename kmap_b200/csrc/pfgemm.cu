@@ -37,6 +37,9 @@
 
 #include <string.h>
 
+#include <algorithm>
+#include <cmath>
+
 #include <atomic>
 #include <mutex>
 #include <vector>
@@ -278,6 +281,140 @@ k_pf_gemm_tc(const __grid_constant__ CUtensorMap amap, const __grid_constant__ C
     }
 }
 
+// ------------------------------------------------- skinny (few rows) ----
+//
+// Decode of many sequences at once (one row per sequence, R <= 128): the
+// operands swap roles so the weight fills the MMA's 128-row side.  A CTA
+// owns 128 columns of Y (the rows of Wt, A) against all R rows of x (B, the
+// MMA's N = RN, R rounded up; rows past R read zeros) over one range of K
+// blocks (split K: gridDim.y ranges, their partial tiles summed in range
+// order by k_bd_ksum).  TMEM holds the 128 x RN fp32 tile: lane = column of
+// Y, TMEM column = row of x.  Stages of 16 KB of weight + TERMS x RN x 128
+// bytes of x; two CTAs per SM keep 2 x STAGES weight boxes in flight.
+
+template <int TERMS, int RN>
+struct BDGeom {
+    static constexpr int BM = 128, BK = 64;
+    static constexpr int A_BYTES = BM * BK * 2;      // weight box (128 columns of Y)
+    static constexpr int B_BYTES = RN * BK * 2;      // one term's box of x
+    static constexpr int STAGE_BYTES = A_BYTES + TERMS * B_BYTES;
+    static constexpr int THREADS = 192;
+    // as many stages as fit two CTAs in an SM's 228 KB (at least 2)
+    static constexpr int FIT = (113 * 1024 - 1280) / STAGE_BYTES;
+    static constexpr int STAGES = FIT < 2 ? 2 : FIT > 8 ? 8 : FIT;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int TERMS, int RN>
+__global__ void __launch_bounds__(192, 2)
+k_bd_gemm_tc(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+             int R, int K, int N, int kb_per, float *__restrict__ out, int *status) {
+    using G = BDGeom<TERMS, RN>;
+    constexpr int STAGES = G::STAGES;
+    static_assert(RN % 32 == 0 && RN <= 128, "x rows per tile: 32, 64 or 128");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * G::STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *done = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * G::BM;
+    const int nk = K / G::BK;
+    const int kb0 = blockIdx.y * kb_per, kb1 = min(nk, kb0 + kb_per), nkb = kb1 - kb0;
+    out += (size_t)blockIdx.y * R * N;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {   // TMEM accumulator: RN fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(RN) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {   // ------------------------------------ producer
+            prefetch_tmap(&wmap);
+            prefetch_tmap(&xmap);
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, status)) break;
+                uint8_t *st = smem + s * G::STAGE_BYTES;
+                const int kx = (kb0 + i) * G::BK;
+                mbar_expect_tx(&full[s], G::STAGE_BYTES);
+                tma_load_2d(st, &wmap, kx, n0, &full[s]);
+#pragma unroll
+                for (int t = 0; t < TERMS; t++)
+                    tma_load_3d(st + G::A_BYTES + t * G::B_BYTES, &xmap, kx, 0, t, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {   // ------------------------------------ MMA issue
+            constexpr uint32_t idesc = umma_idesc_bf16(128, RN);
+            for (int i = 0; i < nkb; i++) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&full[s], (i / STAGES) & 1, status)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * G::STAGE_BYTES);
+                const uint32_t sb = sa + G::A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < G::BK / 16; kk++)
+#pragma unroll
+                    for (int t = 0; t < TERMS; t++)
+                        umma_bf16(tmem, umma_desc_sw128(sa + 32 * kk),
+                                  umma_desc_sw128(sb + t * G::B_BYTES + 32 * kk), idesc,
+                                  (i | kk | t) != 0 ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(done);
+        }
+    } else {   // ---------------------------------------------- epilogue
+        const int q = warp & 3;                  // TMEM lane quarter: columns 32q .. 32q + 31
+        const int n = n0 + 32 * q + lane;
+        const bool ok = mbar_wait(done, 0, status) && nkb > 0;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < RN; c0 += 32) {
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+            if (!ok) continue;
+#pragma unroll
+            for (int i = 0; i < 32; i++)   // lanes write 32 consecutive columns of row c0 + i
+                if (c0 + i < R) out[(size_t)(c0 + i) * N + n] = v[i];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(RN)
+                     : "memory");
+    }
+}
+
+// y[i] = part[0][i] + part[1][i] + ... (the K ranges in order)
+__global__ void k_bd_ksum(const float *__restrict__ part, int ks, long long n,
+                          float *__restrict__ y) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float a = part[i];
+        for (int z = 1; z < ks; z++) a = __fadd_rn(a, part[(size_t)z * n + i]);
+        y[i] = a;
+    }
+}
+
 // x -> TERMS bf16 planes: hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid)
 // (round to nearest even; each difference exact in fp32).
 template <int TERMS>
@@ -382,6 +519,86 @@ bool pf_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, co
                 : launch_pf<2, 128, 4>(s, am, bm, R, K, N, y, status);
 }
 
+// K ranges of the skinny kernel for a 128-column-tile count: the smallest
+// split whose CTAs fill the 148 SMs (two CTAs each) to at least 85 %, every
+// range at least 4 K blocks.
+int bd_gemm_splits(int K, int N) {
+    const int nk = K / 64, tiles = N / 128;
+    int best = 1;
+    double best_eff = 0;
+    for (int ks = 1; ks <= 16 && nk / ks >= 4; ks++) {
+        const int per = (nk + ks - 1) / ks, real = (nk + per - 1) / per;
+        const double waves = (double)tiles * real / (2 * 148);
+        const double eff = waves / std::ceil(waves);
+        if (eff > best_eff + 1e-9) {
+            best = real;
+            best_eff = eff;
+        }
+        if (eff >= 0.85) break;
+    }
+    return best;
+}
+
+template <int TERMS, int RN>
+static bool launch_bd(cudaStream_t s, const CUtensorMap &wm, const CUtensorMap &xm, int R, int K,
+                      int N, int per, int nz, float *out, int *status) {
+    using G = BDGeom<TERMS, RN>;
+    auto kern = k_bd_gemm_tc<TERMS, RN>;
+    static std::atomic<bool> attr[64] = {};
+    int dev = 0;
+    if (!KLLM_CUDA(cudaGetDevice(&dev))) return false;
+    if (!attr[dev & 63].load()) {
+        if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            G::SMEM)))
+            return false;
+        attr[dev & 63].store(true);
+    }
+    dim3 grid(N / 128, nz);
+    kern<<<grid, G::THREADS, G::SMEM, s>>>(wm, xm, R, K, N, per, out, status);
+    g_launches++;
+    return KLLM_CUDA(cudaGetLastError());
+}
+
+bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
+                int N, float *y, float *part, int *status) {
+    if (!pf_gemm_applies(K, N) || R <= 0 || R > 128 || (terms != 2 && terms != 3) ||
+        (reinterpret_cast<uintptr_t>(xs_bf16) & 15) || (reinterpret_cast<uintptr_t>(wt_bf16) & 15)) {
+        set_error("bd_gemm_tc: unsupported shape or alignment (R %d, K %d, N %d)", R, K, N);
+        return false;
+    }
+    const int ks = bd_gemm_splits(K, N);
+    if (ks > 1 && !part) {
+        set_error("bd_gemm_tc: %d K ranges need a partial-sum buffer", ks);
+        return false;
+    }
+    CUtensorMap wm, xm;
+    const int RN = R <= 32 ? 32 : R <= 64 ? 64 : 128;
+    const cuuint64_t wdims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    const cuuint64_t wstr[1] = {(cuuint64_t)K * 2};
+    const cuuint64_t xdims[3] = {(cuuint64_t)K, (cuuint64_t)R, (cuuint64_t)terms};
+    const cuuint64_t xstr[2] = {(cuuint64_t)K * 2, (cuuint64_t)R * K * 2};
+    if (!bf16_tmap(&wm, wt_bf16, 2, wdims, wstr, 128) ||
+        !bf16_tmap(&xm, xs_bf16, 3, xdims, xstr, RN))
+        return false;
+    // ranges of `per` K blocks; nz <= ks of them (the partial buffer's count)
+    const int nk = K / 64, per = (nk + ks - 1) / ks, nz = (nk + per - 1) / per;
+    float *out = nz > 1 ? part : y;
+    bool ok;
+    if (terms == 3)
+        ok = RN == 32 ? launch_bd<3, 32>(s, wm, xm, R, K, N, per, nz, out, status)
+           : RN == 64 ? launch_bd<3, 64>(s, wm, xm, R, K, N, per, nz, out, status)
+                      : launch_bd<3, 128>(s, wm, xm, R, K, N, per, nz, out, status);
+    else
+        ok = RN == 32 ? launch_bd<2, 32>(s, wm, xm, R, K, N, per, nz, out, status)
+           : RN == 64 ? launch_bd<2, 64>(s, wm, xm, R, K, N, per, nz, out, status)
+                      : launch_bd<2, 128>(s, wm, xm, R, K, N, per, nz, out, status);
+    if (!ok || nz == 1) return ok;
+    const long long n = (long long)R * N;
+    k_bd_ksum<<<(int)std::min<long long>((n + 255) / 256, 148 * 8), 256, 0, s>>>(part, nz, n, y);
+    g_launches++;
+    return KLLM_CUDA(cudaGetLastError());
+}
+
 }  // namespace kllm
 
 using namespace kllm;
@@ -413,21 +630,28 @@ extern "C" int kllm_tt_gemm_tc(const float *x, int rows, const float *codebook, 
             return -1;
         }
     }
+    // few rows: the weight on the MMA's 128-row side, K split over ranges
+    const bool skinny = rows <= 64;
+    const int ks = skinny ? bd_gemm_splits(K, N) : 1;
     void *xs = nullptr, *wt = nullptr;
+    float *part = nullptr;
     int *st = nullptr;
     bool ok = KLLM_CUDA(cudaMallocAsync(&xs, (size_t)terms * rows * K * 2, s)) &&
               KLLM_CUDA(cudaMallocAsync(&wt, (size_t)N * K * 2, s)) &&
               KLLM_CUDA(cudaMallocAsync((void **)&st, 4, s)) &&
+              (ks == 1 || KLLM_CUDA(cudaMallocAsync((void **)&part, (size_t)ks * rows * N * 4, s))) &&
               KLLM_CUDA(cudaMemsetAsync(st, 0, 4, s)) &&
               pf_build_wt(s, idx, codebook, K, N, wt) &&
               pf_split(s, x, (long long)rows * K, terms, xs) &&
-              pf_gemm_tc(s, xs, terms, rows, K, wt, N, y, st);
+              (skinny ? bd_gemm_tc(s, xs, terms, rows, K, wt, N, y, part, st)
+                      : pf_gemm_tc(s, xs, terms, rows, K, wt, N, y, st));
     int status = 0;
     if (ok) ok = KLLM_CUDA(cudaMemcpyAsync(&status, st, 4, cudaMemcpyDeviceToHost, s)) &&
                  KLLM_CUDA(cudaStreamSynchronize(s));
     if (xs) cudaFreeAsync(xs, s);
     if (wt) cudaFreeAsync(wt, s);
     if (st) cudaFreeAsync(st, s);
+    if (part) cudaFreeAsync(part, s);
     if (ok && status) {
         set_error("kllm_tt_gemm_tc: kernel reported status 0x%x (a wait timed out)", status);
         ok = false;

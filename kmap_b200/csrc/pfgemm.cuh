@@ -18,4 +18,12 @@ bool pf_split(cudaStream_t s, const float *x, long long n, int terms, void *xs_b
 bool pf_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
                 int N, float *y, int *status);
 
+// Few rows (R <= 128, decode of many sequences): the weight on the MMA's
+// 128-row side, K split over bd_gemm_splits(K, N) ranges whose partial
+// tiles (part: that many x R x N floats; unused for one range) are summed
+// in order into y.
+int bd_gemm_splits(int K, int N);
+bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
+                int N, float *y, float *part, int *status);
+
 }  // namespace kllm

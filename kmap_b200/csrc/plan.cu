@@ -519,6 +519,7 @@ struct DecodePlan {
     // tensor-core projections: per layer the bf16 weights transposed
     // ([N][K], 4 per layer: qkv, o, gate_up, down), built at the first pass
     std::vector<void *> pf_wt;
+    bool pf_wt_tried = false;
     int pf_terms = 0;    // bf16 terms of x (0: the exact FP32 TT-GEMM)
     // batched decode of several sequences: caches and rows, grown as needed
     float *bd_arena = nullptr;
@@ -1270,6 +1271,41 @@ static bool ensure_graph(CtxImpl *c, DecodePlan *p) {
     return true;
 }
 
+// The layers' projection weights as bf16 Wt[N][K] for the tensor-core
+// GEMMs, built once per plan, when the plan's value streams are bf16 (every
+// codebook entry a bf16 number) and every projection's shape fits; pf_wt
+// stays empty otherwise.  False only on a CUDA error.
+static bool plan_layer_wt(CtxImpl *c, DecodePlan *p, cudaStream_t s) {
+    if (!p->pf_wt.empty() || p->pf_wt_tried) return true;
+    p->pf_wt_tried = true;
+    const TemplateInfo &t = p->ti;
+    const TapeCtx *ctx = &c->base;
+    bool tc = p->vm == TTX_VBF16;
+    for (int l = 0; tc && l < t.L; l++)
+        for (int sl : {t.layers[l].qkv, t.layers[l].o, t.layers[l].gu, t.layers[l].dn})
+            tc = tc && pf_gemm_applies(ctx->slots[sl].tt_K, ctx->slots[sl].tt_N);
+    if (!tc) return true;
+    p->pf_wt.assign((size_t)4 * t.L, nullptr);
+    for (int l = 0; l < t.L; l++) {
+        const LayerSlots &ls = t.layers[l];
+        const int mats[4] = {ls.qkv, ls.o, ls.gu, ls.dn};
+        for (int i = 0; i < 4; i++) {
+            const Slot &sl = ctx->slots[mats[i]];
+            const DevSlot &w = c->ds[mats[i]];
+            void *&wt = p->pf_wt[(size_t)4 * l + i];
+            if (!KLLM_CUDA(cudaMalloc(&wt, (size_t)sl.tt_K * sl.tt_N * 2)) ||
+                !pf_build_wt(s, w.d_idx, w.d_cb, sl.tt_K, sl.tt_N, wt)) {
+                cudaStreamSynchronize(s);
+                for (void *b : p->pf_wt)
+                    if (b) cudaFree(b);
+                p->pf_wt.clear();
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 // Batched prompt pass (KLLM infer option `prefill`): positions 0..R-1 of
 // the prompt through every layer at once -- projections as TT-GEMMs (rows
 // bit-identical to the TT-GEMV), norms, RoPE, causal attention, residuals
@@ -1294,28 +1330,11 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, const int *prompt_dev
     // plan's value streams are bf16) and the shapes fit; KLLM_PREFILL_TC=0
     // keeps the exact FP32 TT-GEMM, KLLM_PREFILL_TERMS picks 2 or 3 (the
     // default) bf16 terms of x.
-    if (p->pf_terms == 0 && p->pf_wt.empty()) {
-        bool tc = env_on("KLLM_PREFILL_TC", true) && p->vm == TTX_VBF16;
-        for (int l = 0; tc && l < L; l++)
-            for (int sl : {t.layers[l].qkv, t.layers[l].o, t.layers[l].gu, t.layers[l].dn})
-                tc = tc && pf_gemm_applies(ctx->slots[sl].tt_K, ctx->slots[sl].tt_N);
-        if (tc) {
+    if (p->pf_terms == 0 && env_on("KLLM_PREFILL_TC", true)) {
+        if (!plan_layer_wt(c, p, s)) return false;
+        if (!p->pf_wt.empty()) {
             const char *te = getenv("KLLM_PREFILL_TERMS");
-            const int terms = te && atoi(te) == 2 ? 2 : 3;
-            p->pf_wt.assign((size_t)4 * L, nullptr);
-            for (int l = 0; l < L && tc; l++) {
-                const LayerSlots &ls = t.layers[l];
-                const int mats[4] = {ls.qkv, ls.o, ls.gu, ls.dn};
-                for (int i = 0; i < 4 && tc; i++) {
-                    const Slot &sl = ctx->slots[mats[i]];
-                    const DevSlot &w = c->ds[mats[i]];
-                    void *&wt = p->pf_wt[(size_t)4 * l + i];
-                    tc = KLLM_CUDA(cudaMalloc(&wt, (size_t)sl.tt_K * sl.tt_N * 2)) &&
-                         pf_build_wt(s, w.d_idx, w.d_cb, sl.tt_K, sl.tt_N, wt);
-                }
-            }
-            if (!tc) return false;
-            p->pf_terms = terms;
+            p->pf_terms = te && atoi(te) == 2 ? 2 : 3;
         }
     }
     // arena: hA, hB, xn [R][H]; big [R][max(nq, 2F, H)]; qr, cx [R][qd];
@@ -1452,19 +1471,45 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         total += lens[i];
     }
     cudaStream_t s = c->stream;
-    const bool tc = env_on("KLLM_BATCH_TC", false) && p->vm == TTX_VBF16;
+    // tensor-core projections by default when the codebooks are bf16 numbers
+    // (KLLM_BATCH_TC=0: the exact FP32 TT-GEMM, each row bit-identical to
+    // the TT-GEMV)
+    bool tc = env_on("KLLM_BATCH_TC", true) && p->vm == TTX_VBF16 && nseq <= 128;
+    if (tc && !plan_layer_wt(c, p, s)) return false;
+    const Slot &lms = ctx->slots[t.lm];
+    const bool layer_tc = tc && !p->pf_wt.empty();
+    const bool lm_tc = tc && pf_gemm_applies(lms.tt_K, lms.tt_N);
+    // split-K partial tiles of the skinny tensor-core GEMM
+    size_t part_n = 0;
+    if (tc) {
+        const LayerSlots &l0 = t.layers[0];
+        for (int sl : {l0.qkv, l0.o, l0.gu, l0.dn, t.lm}) {
+            const Slot &x = ctx->slots[sl];
+            if (!pf_gemm_applies(x.tt_K, x.tt_N)) continue;
+            const int ks = bd_gemm_splits(x.tt_K, x.tt_N);
+            if (ks > 1) part_n = std::max(part_n, (size_t)ks * nseq * x.tt_N);
+        }
+    }
+    const size_t att_smem = bd_att_smem(t.groups, hd, mp);
+    if (att_smem > 227 * 1024) {
+        set_error("batched decode: %d positions of %d query heads exceed the attention block's "
+                  "shared memory", mp, t.groups);
+        return false;
+    }
     // arena (floats, each piece a multiple of 4): K and V caches of every
     // sequence; rows h, hB, xn [nseq][H]; big [nseq][max(nq, 2F, H, V)]; qr,
-    // cx [nseq][qd]; act [nseq][F]; bf16 terms of a projection's input; ints:
-    // prompts, tokens, positions, generated tokens
+    // cx [nseq][qd]; act [nseq][F]; bf16 terms of a projection's input;
+    // split-K partials; ints: prompts, tokens, positions, first positions,
+    // generated tokens
     auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t seq_stride = (size_t)L * nkv * mp * hd;
     const size_t kv = up4((size_t)nseq * seq_stride);
     const size_t rh = up4((size_t)nseq * H), rq = up4((size_t)nseq * qd), rf = up4((size_t)nseq * F);
     const size_t wide = up4((size_t)nseq * std::max({(size_t)nq, (size_t)2 * F, (size_t)H, (size_t)V}));
     const size_t rxs = up4(((size_t)3 * nseq * std::max({(size_t)H, (size_t)F, (size_t)qd}) + 1) / 2);
-    const size_t ints = up4(total + 2 * (size_t)nseq + (size_t)nseq * max_new);
-    const size_t need = 2 * kv + 3 * rh + wide + 2 * rq + rf + rxs + ints;
+    const size_t rpart = up4(part_n);
+    const size_t ints = up4(total + 3 * (size_t)nseq + (size_t)nseq * max_new);
+    const size_t need = 2 * kv + 3 * rh + wide + 2 * rq + rf + rxs + rpart + ints;
     if (p->bd_cap < need) {
         if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
         if (p->bd_arena) cudaFree(p->bd_arena);
@@ -1474,9 +1519,10 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         p->bd_cap = need;
     }
     float *kcs = p->bd_arena, *vcs = kcs + kv, *h = vcs + kv, *hB = h + rh, *xn = hB + rh,
-          *big = xn + rh, *qr = big + wide, *cx = qr + rq, *act = cx + rq, *xs = act + rf;
-    int *d_prompts = reinterpret_cast<int *>(xs + rxs), *d_tok = d_prompts + total,
-        *d_pos = d_tok + nseq, *d_gen = d_pos + nseq;
+          *big = xn + rh, *qr = big + wide, *cx = qr + rq, *act = cx + rq, *xs = act + rf,
+          *part = xs + rxs;
+    int *d_prompts = reinterpret_cast<int *>(part + rpart), *d_tok = d_prompts + total,
+        *d_pos = d_tok + nseq, *d_start = d_pos + nseq, *d_gen = d_start + nseq;
     std::vector<int> tok0(nseq), pos0(nseq);
     {
         size_t off = 0;
@@ -1489,11 +1535,10 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
     if (!KLLM_CUDA(cudaMemcpyAsync(d_prompts, prompts, total * 4, cudaMemcpyHostToDevice, s)) ||
         !KLLM_CUDA(cudaMemcpyAsync(d_tok, tok0.data(), nseq * 4, cudaMemcpyHostToDevice, s)) ||
         !KLLM_CUDA(cudaMemcpyAsync(d_pos, pos0.data(), nseq * 4, cudaMemcpyHostToDevice, s)) ||
+        !KLLM_CUDA(cudaMemcpyAsync(d_start, pos0.data(), nseq * 4, cudaMemcpyHostToDevice, s)) ||
         !KLLM_CUDA(cudaMemsetAsync(p->status, 0, 4, s)))
         return false;
     // the lm_head as bf16 Wt for the tensor-core form (built once)
-    const Slot &lms = ctx->slots[t.lm];
-    const bool lm_tc = tc && pf_gemm_applies(lms.tt_K, lms.tt_N);
     if (lm_tc && !p->bd_lm_wt) {
         if (!KLLM_CUDA(cudaMalloc(&p->bd_lm_wt, (size_t)lms.tt_K * lms.tt_N * 2)) ||
             !pf_build_wt(s, c->ds[t.lm].d_idx, c->ds[t.lm].d_cb, lms.tt_K, lms.tt_N, p->bd_lm_wt))
@@ -1512,7 +1557,6 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         }
     }
     if (!KLLM_CUDA(cudaEventRecord(p->ev1, s))) return false;
-    const bool layer_tc = tc && p->pf_terms > 0;   // the prompt pass built the layers' Wt
     auto gemm = [&](int slot, int layer, int which, const float *x, float *y) {
         const Slot &sl = ctx->slots[slot];
         const DevSlot &w = c->ds[slot];
@@ -1520,49 +1564,68 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
                                    : (lm_tc ? p->bd_lm_wt : nullptr);
         if (wt)
             return pf_split(s, x, (long long)nseq * sl.tt_K, 3, xs) &&
-                   pf_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, y, p->status);
+                   bd_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, y, part, p->status);
         return kllm_tt_gemm(x, nseq, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
     };
     const int ew_blocks = 148 * 8;
-    const size_t att_smem = (size_t)std::max(mp, PF_THREADS) * 4;
+    auto att = hd == 32 ? k_bd_attn_group<32> : hd == 64 ? k_bd_attn_group<64>
+                                                         : k_bd_attn_group<128>;
     if (att_smem > 48 * 1024 &&
-        !KLLM_CUDA(cudaFuncSetAttribute(k_bd_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        !KLLM_CUDA(cudaFuncSetAttribute(att, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)att_smem)))
         return false;
-    bool ok = true;
-    for (int step = 0; ok && step < max_new; step++) {
+    // one decode step of every sequence: positions, tokens and the generated
+    // token's slot are read on the device, so the same launches (a graph)
+    // serve every step
+    auto record_step = [&]() -> bool {
         k_pf_embed<<<nseq, PF_THREADS, 0, s>>>(p->embed, d_tok, H, h);
         g_launches++;
-        for (int l = 0; ok && l < L; l++) {
+        for (int l = 0; l < L; l++) {
             const LayerSlots &ls = t.layers[l];
             float *kc = kcs + (size_t)l * nkv * mp * hd, *vc = vcs + (size_t)l * nkv * mp * hd;
             k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
-            ok = gemm(ls.qkv, l, 0, xn, big);
-            if (!ok) break;
+            if (!gemm(ls.qkv, l, 0, xn, big)) return false;
             k_bd_rope_kv<<<nseq, PF_THREADS, 0, s>>>(big, d_pos, nq, nh, nkv, hd, p->rcos, p->rsin,
                                                      mp, seq_stride, qr, kc, vc);
-            k_bd_attention<<<dim3(nseq, nh), PF_THREADS, att_smem, s>>>(
-                qr, kc, vc, d_pos, nh, t.groups, hd, mp, seq_stride, p->scale, cx);
-            ok = gemm(ls.o, l, 1, cx, big);
-            if (!ok) break;
+            att<<<dim3(nseq, nkv), BD_ATT_THREADS, att_smem, s>>>(
+                qr, kc, vc, d_pos, nh, t.groups, mp, seq_stride, p->scale, cx);
+            if (!gemm(ls.o, l, 1, cx, big)) return false;
             k_pf_add<<<ew_blocks, 256, 0, s>>>(h, big, (long long)nseq * H, hB);
             k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], H,
                                                     xn);
-            ok = gemm(ls.gu, l, 2, xn, big);
-            if (!ok) break;
+            if (!gemm(ls.gu, l, 2, xn, big)) return false;
             k_pf_swiglu<<<ew_blocks, 256, 0, s>>>(big, F, (long long)nseq * F, act);
-            ok = gemm(ls.dn, l, 3, act, big);
-            if (!ok) break;
+            if (!gemm(ls.dn, l, 3, act, big)) return false;
             k_pf_add<<<ew_blocks, 256, 0, s>>>(hB, big, (long long)nseq * H, h);
             g_launches += 7;
         }
-        if (!ok) break;
         k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm.back(), p->f_eps, H, xn);
-        ok = gemm(t.lm, 0, 4, xn, big);
-        if (!ok) break;
-        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(big, V, step, max_new, d_tok, d_pos, d_gen);
+        if (!gemm(t.lm, 0, 4, xn, big)) return false;
+        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(big, V, d_start, max_new, d_tok, d_pos, d_gen);
         g_launches += 3;
-        ok = KLLM_CUDA(cudaGetLastError());
+        return KLLM_CUDA(cudaGetLastError());
+    };
+    bool ok = true;
+    if (c->opts.use_graphs && max_new > 1) {
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        const long long g0 = g_launches;
+        ok = KLLM_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        if (ok) {
+            const bool rec = record_step();
+            ok = KLLM_CUDA(cudaStreamEndCapture(s, &graph)) && rec;
+        }
+        const long long per_step = g_launches - g0;
+        ok = ok && KLLM_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+        for (int step = 0; ok && step < max_new; step++) ok = KLLM_CUDA(cudaGraphLaunch(exec, s));
+        if (ok) g_launches += per_step * (max_new - 1);
+        if (exec) {
+            cudaStreamSynchronize(s);
+            cudaGraphExecDestroy(exec);
+        }
+        if (graph) cudaGraphDestroy(graph);
+    } else {
+        for (int step = 0; ok && step < max_new; step++) ok = record_step();
     }
     if (!ok || !KLLM_CUDA(cudaEventRecord(p->ev2, s))) return false;
     std::vector<int> gen((size_t)nseq * max_new);

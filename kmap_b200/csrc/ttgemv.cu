@@ -267,8 +267,9 @@ struct GemvScratch {
     size_t cap = 0;
     int *counters = nullptr;
     size_t ccap = 0;
-    int *status = nullptr;          // device status word of the fused kernel
-    int *status_host = nullptr;     // pinned copy, refreshed after every launch
+    int *status = nullptr;          // device alias of status_host (the kernel's status word)
+    int *status_host = nullptr;     // mapped pinned word: the kernel flags a wait that
+                                    // gave up here directly (no copy after each launch)
 };
 static std::mutex g_scratch_mu;
 static GemvScratch g_scratch[64];
@@ -278,11 +279,15 @@ static bool scratch_for(int dev, size_t floats, size_t ncount, float **part, int
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     GemvScratch &s = g_scratch[dev & 63];
     if (!s.status) {
-        if (!KLLM_CUDA(cudaMalloc((void **)&s.status, sizeof(int))) ||
-            !KLLM_CUDA(cudaMemset(s.status, 0, sizeof(int))) ||
-            !KLLM_CUDA(cudaHostAlloc((void **)&s.status_host, sizeof(int), cudaHostAllocDefault)))
+        if (!KLLM_CUDA(cudaHostAlloc((void **)&s.status_host, sizeof(int),
+                                     cudaHostAllocMapped | cudaHostAllocPortable)))
             return false;
         *s.status_host = 0;
+        if (!KLLM_CUDA(cudaHostGetDevicePointer((void **)&s.status, s.status_host, 0))) {
+            cudaFreeHost(s.status_host);
+            s.status_host = nullptr;
+            return false;
+        }
     }
     *status = s.status;
     *status_host = s.status_host;
@@ -332,19 +337,16 @@ extern "C" int kllm_tt_gemv(const float *x, int rows, const float *codebook, int
                      &status_host))
         return -1;
     // A wait of an earlier call's kernel that gave up (its y columns are
-    // NaN) is reported here, once: the pinned copy of the status word is
-    // refreshed on the stream after every fused launch.
+    // NaN) is reported here, once: the kernel writes the mapped pinned
+    // status word itself.
     if (const int st = *reinterpret_cast<volatile int *>(status_host)) {
         *reinterpret_cast<volatile int *>(status_host) = 0;
-        cudaMemsetAsync(status, 0, sizeof(int), s);
         set_error("kllm_tt_gemv: an earlier call's kernel reported status 0x%x (a wait timed "
                   "out; its y holds NaN)", st);
         return -1;
     }
     if (rows == 1 && tf_tma_ok(idx, codebook, K, N, n_codes, tf_config(K, N, n_codes, E_Y)))
-        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, part, counters, y, status) &&
-                       KLLM_CUDA(cudaMemcpyAsync(status_host, status, sizeof(int),
-                                                 cudaMemcpyDeviceToHost, s))
+        return tt_gemv_fused_y(s, x, codebook, n_codes, idx, K, N, part, counters, y, status)
                    ? 0
                    : -1;
     if (!tt_gemv_partials(s, x, rows, codebook, n_codes, idx, K, N, part)) return -1;

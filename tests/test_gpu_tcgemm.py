@@ -7,7 +7,8 @@ TT-GEMM (kllm_tt_gemm): with 3 terms the error is the tensor core's fp32
 accumulation (a few 1e-6 of the row's sum of |x w|); with 2 terms x itself
 is carried to 2^-17.  Shapes: one and several 128-row tiles,
 ragged row counts (the tensor map fills rows past the end with zeros and the
-epilogue skips them), N multiples of 128 and 256, K = 64 .. 5632."""
+epilogue skips them), N multiples of 128 and 256, K = 64 .. 14336; up to
+64 rows (decode of several sequences) through the split-K form."""
 import numpy as np
 import pytest
 
@@ -48,7 +49,11 @@ def _run(fn, x, cb, idx, *extra):
 
 
 @pytest.mark.parametrize("R,K,N", [(128, 64, 128), (128, 2048, 256), (200, 1024, 384),
-                                   (1, 2048, 2048), (300, 5632, 256), (513, 2048, 2560)])
+                                   (1, 2048, 2048), (300, 5632, 256), (513, 2048, 2560),
+                                   # few rows (<= 64): the weight on the MMA's 128-row
+                                   # side, K split over ranges summed in order
+                                   (32, 4096, 6144), (17, 14336, 4096), (64, 4096, 28672),
+                                   (5, 1024, 128), (33, 256, 640)])
 @pytest.mark.parametrize("terms", [3, 2])
 def test_tc_gemm_against_float64(gpu, R, K, N, terms):
     import kmap_b200
