@@ -15,6 +15,14 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: full-size model runs (minutes)")
 
 
+def pytest_collection_modifyitems(config, items):
+    # A GPU test that runs past 10 minutes ends the run (stack dump, exit)
+    # instead of holding the device.
+    for item in items:
+        if item.get_closest_marker("gpu") and not item.get_closest_marker("timeout"):
+            item.add_marker(pytest.mark.timeout(600, method="thread"))
+
+
 @pytest.fixture(scope="session")
 def oracle():
     import harness
