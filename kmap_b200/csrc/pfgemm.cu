@@ -540,19 +540,31 @@ int bd_gemm_splits(int K, int N) {
 }
 
 template <int TERMS, int RN>
+static bool bd_attr(int dev) {
+    static std::atomic<bool> attr[64] = {};
+    if (attr[dev & 63].load()) return true;
+    if (!KLLM_CUDA(cudaFuncSetAttribute(k_bd_gemm_tc<TERMS, RN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BDGeom<TERMS, RN>::SMEM)))
+        return false;
+    attr[dev & 63].store(true);
+    return true;
+}
+
+bool bd_gemm_prepare() {
+    int dev = 0;
+    return KLLM_CUDA(cudaGetDevice(&dev)) && bd_attr<3, 32>(dev) && bd_attr<3, 64>(dev) &&
+           bd_attr<3, 128>(dev) && bd_attr<2, 32>(dev) && bd_attr<2, 64>(dev) &&
+           bd_attr<2, 128>(dev);
+}
+
+template <int TERMS, int RN>
 static bool launch_bd(cudaStream_t s, const CUtensorMap &wm, const CUtensorMap &xm, int R, int K,
                       int N, int per, int nz, float *out, int *status) {
     using G = BDGeom<TERMS, RN>;
     auto kern = k_bd_gemm_tc<TERMS, RN>;
-    static std::atomic<bool> attr[64] = {};
     int dev = 0;
-    if (!KLLM_CUDA(cudaGetDevice(&dev))) return false;
-    if (!attr[dev & 63].load()) {
-        if (!KLLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            G::SMEM)))
-            return false;
-        attr[dev & 63].store(true);
-    }
+    if (!KLLM_CUDA(cudaGetDevice(&dev)) || !bd_attr<TERMS, RN>(dev)) return false;
     dim3 grid(N / 128, nz);
     kern<<<grid, G::THREADS, G::SMEM, s>>>(wm, xm, R, K, N, per, out, status);
     g_launches++;

@@ -23,6 +23,9 @@ bool pf_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, co
 // tiles (part: that many x R x N floats; unused for one range) are summed
 // in order into y.
 int bd_gemm_splits(int K, int N);
+// Kernel attributes of every few-row instance set up front (before a graph
+// capture of its launches).
+bool bd_gemm_prepare();
 bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
                 int N, float *y, float *part, int *status);
 

@@ -1578,6 +1578,7 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
                    bd_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, y, part, p->status);
         return kllm_tt_gemm(x, nseq, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
     };
+    if (tc && !bd_gemm_prepare()) return false;
     const int ew_blocks = 148 * 8;
     auto att = hd == 32 ? k_bd_attn_group<32> : hd == 64 ? k_bd_attn_group<64>
                                                          : k_bd_attn_group<128>;
