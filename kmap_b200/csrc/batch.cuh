@@ -1,35 +1,114 @@
 // batch.cuh -- the row kernels of batched greedy decode (plan.cu,
 // plan_infer_batch): one row per sequence, every sequence at its own
-// position with its own KV cache.  The projections around them are the
-// prompt pass's GEMMs (bit-exact TT-GEMM per row, or the tensor cores);
-// norms, residual adds and SwiGLU are the prompt pass's row kernels.  Each
-// element is the tape's float arithmetic for its sequence (reductions in a
-// fixed order of their own, as in the prompt pass).
+// position with its own KV cache.  Around the projections (the few-row
+// tensor-core GEMM, or the bit-exact TT-GEMM per row) each kernel does
+// the whole stretch between two of them: it reads the previous GEMM's
+// output as the sum of its K-range partial tiles (in range order), applies
+// the tape's float arithmetic of that stretch (RMSNorm, RoPE + cache
+// append, attention, residual add, SwiGLU), and writes the next GEMM's
+// input directly -- fp32 rows, or the three bf16 terms of the exact split
+// the tensor cores take.  Reductions run in a fixed order of their own, as
+// in the prompt pass.
 #pragma once
+
+#include <cuda_bf16.h>
 
 #include "common.cuh"
 #include "prefill.cuh"
 
 namespace kllm {
 
-// Row r of the fused QKV output at position pos[r]: rotate-half RoPE of q
+// One element of a GEMM output: the sum of its nz K-range partial tiles,
+// part[z * plane + i], in range order (nz = 1: the output itself).
+__device__ __forceinline__ float bd_sum(const float *__restrict__ part, int nz, size_t plane,
+                                        size_t i) {
+    float a = part[i];
+    for (int z = 1; z < nz; z++) a = __fadd_rn(a, part[(size_t)z * plane + i]);
+    return a;
+}
+
+// One element of the next GEMM's input: fp32 (terms 0), or the bf16 terms
+// hi = bf16(v), mid = bf16(v - hi), lo = bf16(v - hi - mid), term t at
+// t * plane + i.
+__device__ __forceinline__ void bd_emit(float v, size_t i, int terms, size_t plane,
+                                        void *__restrict__ xs) {
+    if (!terms) {
+        reinterpret_cast<float *>(xs)[i] = v;
+        return;
+    }
+    __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(xs);
+    float r = v;
+    for (int t = 0; t < terms; t++) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(r);
+        o[(size_t)t * plane + i] = b;
+        r = __fsub_rn(r, __bfloat162float(b));
+    }
+}
+
+// Row r: x = res[r] + (the GEMM output's row, or nothing when part is
+// null; with res null, the embedding row of tok[r]); hout[r] = x; then
+// the tape's RMSNORM -- sum of squares, mean as sum * (1 / H) + eps, rsqrt
+// in double, two rounded products -- into the next GEMM's input.
+// (grid: nseq blocks, PF_THREADS threads)
+__global__ void k_bd_add_norm(const float *__restrict__ res, const float *__restrict__ embed,
+                              const int *__restrict__ tok, const float *__restrict__ part, int nz,
+                              const float *__restrict__ w, float eps, int H,
+                              float *__restrict__ hout, int terms, void *__restrict__ xs) {
+    __shared__ float red[PF_THREADS / 32];
+    const int r = blockIdx.x;
+    const size_t plane = (size_t)gridDim.x * H;
+    const float *src = res ? res + (size_t)r * H : embed + (size_t)tok[r] * H;
+    float *hr = hout + (size_t)r * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += PF_THREADS) {
+        float v = src[i];
+        if (part) v = __fadd_rn(v, bd_sum(part, nz, plane, (size_t)r * H + i));
+        hr[i] = v;
+        ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+    const float tot = pf_block_sum(ss, red);
+    const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)H), eps);
+    const float rsq = (float)(1.0 / sqrt((double)add));
+    for (int i = threadIdx.x; i < H; i += PF_THREADS)   // this thread's own writes above
+        bd_emit(__fmul_rn(__fmul_rn(hr[i], rsq), w[i]), (size_t)r * H + i, terms, plane, xs);
+}
+
+// act[r][n] = silu(gate) * up, gate = column n and up = column F + n of the
+// gate_up GEMM's row r (silu in double as the tape's SILU), into the down
+// GEMM's input.  (grid-stride over nseq * F)
+__global__ void k_bd_swiglu(const float *__restrict__ part, int nz, int nseq, int F, int terms,
+                            void *__restrict__ xs) {
+    const long long rf = (long long)nseq * F;
+    const size_t plane = (size_t)nseq * 2 * F;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rf;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / F, n = i % F;
+        const double dg = (double)bd_sum(part, nz, plane, (size_t)(r * 2 * F + n));
+        const float up = bd_sum(part, nz, plane, (size_t)(r * 2 * F + F + n));
+        bd_emit(__fmul_rn((float)(dg / (1.0 + exp(-dg))), up), (size_t)i, terms, (size_t)rf, xs);
+    }
+}
+
+// Row r of the QKV GEMM output at position pos[r]: rotate-half RoPE of q
 // (to q_out[r]) and k, k and v appended to sequence r's cache (row pos[r]).
 // Caches: [seq][layer][kv_head][max_pos][hd]; kc / vc point at this layer of
 // sequence 0, seq_stride floats apart.  (grid: nseq blocks)
-__global__ void k_bd_rope_kv(const float *__restrict__ qkv, const int *__restrict__ pos, int nq,
-                             int nh, int nkv, int hd, const float *__restrict__ rcos,
+__global__ void k_bd_rope_kv(const float *__restrict__ part, int nz, const int *__restrict__ pos,
+                             int nq, int nh, int nkv, int hd, const float *__restrict__ rcos,
                              const float *__restrict__ rsin, int max_pos, size_t seq_stride,
                              float *__restrict__ q_out, float *__restrict__ kc,
                              float *__restrict__ vc) {
     const int r = blockIdx.x, p = pos[r];
     const int qd = nh * hd, kvd = nkv * hd;
-    const float *y = qkv + (size_t)r * nq;
+    const size_t plane = (size_t)gridDim.x * nq, row = (size_t)r * nq;
     float *kr = kc + (size_t)r * seq_stride, *vr = vc + (size_t)r * seq_stride;
     for (int n = threadIdx.x; n < qd + 2 * kvd; n += blockDim.x) {
+        const float y = bd_sum(part, nz, plane, row + n);
         if (n < qd + kvd) {
             const int head = n / hd, dim = n % hd, half = hd / 2;
-            const float pk = dim < half ? -y[n + half] : y[n - half];
-            const float v = __fadd_rn(__fmul_rn(y[n], rcos[(size_t)p * hd + dim]),
+            const float pk = dim < half ? -bd_sum(part, nz, plane, row + n + half)
+                                        : bd_sum(part, nz, plane, row + n - half);
+            const float v = __fadd_rn(__fmul_rn(y, rcos[(size_t)p * hd + dim]),
                                       __fmul_rn(pk, rsin[(size_t)p * hd + dim]));
             if (head < nh)
                 q_out[(size_t)r * qd + n] = v;
@@ -37,7 +116,7 @@ __global__ void k_bd_rope_kv(const float *__restrict__ qkv, const int *__restric
                 kr[((size_t)(head - nh) * max_pos + p) * hd + dim] = v;
         } else {
             const int vi = n - qd - kvd;
-            vr[((size_t)(vi / hd) * max_pos + p) * hd + vi % hd] = y[n];
+            vr[((size_t)(vi / hd) * max_pos + p) * hd + vi % hd] = y;
         }
     }
 }
@@ -49,8 +128,9 @@ __global__ void k_bd_rope_kv(const float *__restrict__ qkv, const int *__restric
 // its dims, then the xor-shuffle tree over the lanes, times the scale.
 // Softmax of query head j by warp j: max, exp in double of the difference,
 // the lanes' serial sums then the tree, division.  P.V: warp w sums its
-// positions serially per dim, the 8 warps' sums added in warp order.
-// Dynamic shared memory: bd_att_smem(groups, HD, max_pos) bytes.
+// positions serially per dim, the 8 warps' sums added in warp order, into
+// the O GEMM's input.  Dynamic shared memory: bd_att_smem(groups, HD,
+// max_pos) bytes.
 constexpr int BD_ATT_THREADS = 256;
 
 __host__ __device__ inline size_t bd_att_smem(int groups, int hd, int max_pos) {
@@ -75,7 +155,7 @@ template <int HD>
 __global__ void __launch_bounds__(BD_ATT_THREADS)
 k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
                 const float *__restrict__ vc, const int *__restrict__ pos, int nh, int groups,
-                int max_pos, size_t seq_stride, float scale, float *__restrict__ ctx) {
+                int max_pos, size_t seq_stride, float scale, int terms, void *__restrict__ xs) {
     constexpr int VEC = HD / 32, NW = BD_ATT_THREADS / 32, U = 4, GB = 8;
     extern __shared__ float bsm[];
     const int r = blockIdx.x, g = blockIdx.y, n = pos[r] + 1;
@@ -169,29 +249,29 @@ k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
         }
     }
     __syncthreads();
-    float *out = ctx + (size_t)r * qd + (size_t)g * groups * HD;
+    const size_t plane = (size_t)gridDim.x * qd, o0 = (size_t)r * qd + (size_t)g * groups * HD;
     for (int i = threadIdx.x; i < groups * HD; i += BD_ATT_THREADS) {
         float o = pv[i];
         for (int w = 1; w < NW; w++) o = __fadd_rn(o, pv[(size_t)w * groups * HD + i]);
-        out[i] = o;
+        bd_emit(o, o0 + i, terms, plane, xs);
     }
 }
 
-// Greedy pick of row r (the reference's: best = logits[0], then strict >
-// over the rest in index order), written as the row's next token and as
+// Greedy pick of row r of the lm_head GEMM output (the reference's: best =
+// logits[0], then strict > over the rest in index order), written as the row's next token and as
 // its generated token pos[r] - start[r]; the row's position advances.
 // (grid: nseq blocks, PF_THREADS threads)
-__global__ void k_bd_argmax(const float *__restrict__ logits, int V, const int *__restrict__ start,
-                            int max_new, int *__restrict__ tok, int *__restrict__ pos,
-                            int *__restrict__ gen) {
+__global__ void k_bd_argmax(const float *__restrict__ part, int nz, int V,
+                            const int *__restrict__ start, int max_new, int *__restrict__ tok,
+                            int *__restrict__ pos, int *__restrict__ gen) {
     __shared__ float bv[PF_THREADS];
     __shared__ int bi[PF_THREADS];
     const int r = blockIdx.x;
-    const float *lg = logits + (size_t)r * V;
+    const size_t plane = (size_t)gridDim.x * V, row = (size_t)r * V;
     float best = -INFINITY;
     int idx = -1;
     for (int v = threadIdx.x; v < V; v += PF_THREADS) {
-        const float x = lg[v];
+        const float x = bd_sum(part, nz, plane, row + v);
         if (x > best) {   // per thread: first maximum in index order (NaN never wins)
             best = x;
             idx = v;
@@ -201,7 +281,7 @@ __global__ void k_bd_argmax(const float *__restrict__ logits, int V, const int *
     bi[threadIdx.x] = idx;
     __syncthreads();
     if (threadIdx.x == 0) {
-        float b = lg[0];
+        float b = bd_sum(part, nz, plane, row);
         int k = 0;
         if (!(b != b)) {   // NaN at 0: the reference keeps index 0
             for (int t = 0; t < PF_THREADS; t++)

@@ -572,7 +572,7 @@ static bool launch_bd(cudaStream_t s, const CUtensorMap &wm, const CUtensorMap &
 }
 
 bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
-                int N, float *y, float *part, int *status) {
+                int N, float *y, float *part, int *status, int *nz_out) {
     if (!pf_gemm_applies(K, N) || R <= 0 || R > 128 || (terms != 2 && terms != 3) ||
         (reinterpret_cast<uintptr_t>(xs_bf16) & 15) || (reinterpret_cast<uintptr_t>(wt_bf16) & 15)) {
         set_error("bd_gemm_tc: unsupported shape or alignment (R %d, K %d, N %d)", R, K, N);
@@ -604,7 +604,8 @@ bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, co
         ok = RN == 32 ? launch_bd<2, 32>(s, wm, xm, R, K, N, per, nz, out, status)
            : RN == 64 ? launch_bd<2, 64>(s, wm, xm, R, K, N, per, nz, out, status)
                       : launch_bd<2, 128>(s, wm, xm, R, K, N, per, nz, out, status);
-    if (!ok || nz == 1) return ok;
+    if (nz_out) *nz_out = nz;
+    if (!ok || nz == 1 || nz_out) return ok;   // nz_out: the caller sums the partial tiles
     const long long n = (long long)R * N;
     k_bd_ksum<<<(int)std::min<long long>((n + 255) / 256, 148 * 8), 256, 0, s>>>(part, nz, n, y);
     g_launches++;

@@ -21,12 +21,13 @@ bool pf_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, co
 // Few rows (R <= 128, decode of many sequences): the weight on the MMA's
 // 128-row side, K split over bd_gemm_splits(K, N) ranges whose partial
 // tiles (part: that many x R x N floats; unused for one range) are summed
-// in order into y.
+// in order into y -- or, with nz_out, left in part for the caller to sum
+// (*nz_out ranges; one range writes y).
 int bd_gemm_splits(int K, int N);
 // Kernel attributes of every few-row instance set up front (before a graph
 // capture of its launches).
 bool bd_gemm_prepare();
 bool bd_gemm_tc(cudaStream_t s, const void *xs_bf16, int terms, int R, int K, const void *wt_bf16,
-                int N, float *y, float *part, int *status);
+                int N, float *y, float *part, int *status, int *nz_out = nullptr);
 
 }  // namespace kllm

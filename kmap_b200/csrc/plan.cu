@@ -1508,19 +1508,19 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         return false;
     }
     // arena (floats, each piece a multiple of 4): K and V caches of every
-    // sequence; rows h, hB, xn [nseq][H]; big [nseq][max(nq, 2F, H, V)]; qr,
-    // cx [nseq][qd]; act [nseq][F]; bf16 terms of a projection's input;
-    // split-K partials; ints: prompts, tokens, positions, first positions,
-    // generated tokens
+    // sequence; residual rows h, hB [nseq][H]; big [nseq][max(nq, 2F, V)]
+    // (a GEMM output in one piece); qr [nseq][qd]; xs, a GEMM's input (fp32
+    // rows or three bf16 terms); split-K partials; ints: prompts, tokens,
+    // positions, first positions, generated tokens
     auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t seq_stride = (size_t)L * nkv * mp * hd;
     const size_t kv = up4((size_t)nseq * seq_stride);
-    const size_t rh = up4((size_t)nseq * H), rq = up4((size_t)nseq * qd), rf = up4((size_t)nseq * F);
+    const size_t rh = up4((size_t)nseq * H), rq = up4((size_t)nseq * qd);
     const size_t wide = up4((size_t)nseq * std::max({(size_t)nq, (size_t)2 * F, (size_t)H, (size_t)V}));
     const size_t rxs = up4(((size_t)3 * nseq * std::max({(size_t)H, (size_t)F, (size_t)qd}) + 1) / 2);
     const size_t rpart = up4(part_n);
     const size_t ints = up4(total + 3 * (size_t)nseq + (size_t)nseq * max_new);
-    const size_t need = 2 * kv + 3 * rh + wide + 2 * rq + rf + rxs + rpart + ints;
+    const size_t need = 2 * kv + 2 * rh + wide + rq + rxs + rpart + ints;
     if (p->bd_cap < need) {
         if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
         if (p->bd_arena) cudaFree(p->bd_arena);
@@ -1529,9 +1529,8 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         if (!dalloc(&p->bd_arena, need)) return false;
         p->bd_cap = need;
     }
-    float *kcs = p->bd_arena, *vcs = kcs + kv, *h = vcs + kv, *hB = h + rh, *xn = hB + rh,
-          *big = xn + rh, *qr = big + wide, *cx = qr + rq, *act = cx + rq, *xs = act + rf,
-          *part = xs + rxs;
+    float *kcs = p->bd_arena, *vcs = kcs + kv, *h = vcs + kv, *hB = h + rh, *big = hB + rh,
+          *qr = big + wide, *xs = qr + rq, *part = xs + rxs;
     int *d_prompts = reinterpret_cast<int *>(part + rpart), *d_tok = d_prompts + total,
         *d_pos = d_tok + nseq, *d_start = d_pos + nseq, *d_gen = d_start + nseq;
     std::vector<int> tok0(nseq), pos0(nseq);
@@ -1568,16 +1567,29 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         }
     }
     if (!KLLM_CUDA(cudaEventRecord(p->ev1, s))) return false;
-    auto gemm = [&](int slot, int layer, int which, const float *x, float *y) {
+    // The projections: the few-row tensor-core GEMM from the bf16 terms in
+    // xs, its K-range partial tiles left in `part` (nz of them; one range
+    // writes `big`), or the exact TT-GEMM from fp32 rows in xs into `big`.
+    // Each returns where its output is and in how many tiles.
+    auto gemm = [&](int slot, int layer, int which, const float **y, int *nz) {
         const Slot &sl = ctx->slots[slot];
         const DevSlot &w = c->ds[slot];
         const void *wt = which < 4 ? (layer_tc ? p->pf_wt[(size_t)4 * layer + which] : nullptr)
                                    : (lm_tc ? p->bd_lm_wt : nullptr);
-        if (wt)
-            return pf_split(s, x, (long long)nseq * sl.tt_K, 3, xs) &&
-                   bd_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, y, part, p->status);
-        return kllm_tt_gemm(x, nseq, w.d_cb, sl.n_codes, w.d_idx, sl.tt_K, sl.tt_N, y, s) == 0;
+        if (wt) {
+            if (!bd_gemm_tc(s, xs, 3, nseq, sl.tt_K, wt, sl.tt_N, big, part, p->status, nz))
+                return false;
+            *y = *nz > 1 ? part : big;
+            return true;
+        }
+        *nz = 1;
+        *y = big;
+        return kllm_tt_gemm(reinterpret_cast<const float *>(xs), nseq, w.d_cb, sl.n_codes,
+                            w.d_idx, sl.tt_K, sl.tt_N, big, s) == 0;
     };
+    // terms of each GEMM's input: 3 for the tensor cores, 0 (fp32) for the
+    // exact TT-GEMM
+    const int lt = layer_tc ? 3 : 0, lmt = lm_tc ? 3 : 0;
     if (tc && !bd_gemm_prepare()) return false;
     const int ew_blocks = 148 * 8;
     auto att = hd == 32 ? k_bd_attn_group<32> : hd == 64 ? k_bd_attn_group<64>
@@ -1588,33 +1600,39 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         return false;
     // one decode step of every sequence: positions, tokens and the generated
     // token's slot are read on the device, so the same launches (a graph)
-    // serve every step
+    // serve every step.  Per layer: QKV GEMM, RoPE + append, attention, O
+    // GEMM, residual add + RMSNorm, gate_up GEMM, SwiGLU, down GEMM, and the
+    // residual add + the next RMSNorm (the next layer's, or the final one).
     auto record_step = [&]() -> bool {
-        k_pf_embed<<<nseq, PF_THREADS, 0, s>>>(p->embed, d_tok, H, h);
+        const float *y = nullptr;
+        int nz = 1;
+        k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(nullptr, p->embed, d_tok, nullptr, 1,
+                                                  p->dev_norm[0], p->eps[0], H, h, lt, xs);
         g_launches++;
         for (int l = 0; l < L; l++) {
             const LayerSlots &ls = t.layers[l];
             float *kc = kcs + (size_t)l * nkv * mp * hd, *vc = vcs + (size_t)l * nkv * mp * hd;
-            k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm[2 * l], p->eps[2 * l], H, xn);
-            if (!gemm(ls.qkv, l, 0, xn, big)) return false;
-            k_bd_rope_kv<<<nseq, PF_THREADS, 0, s>>>(big, d_pos, nq, nh, nkv, hd, p->rcos, p->rsin,
-                                                     mp, seq_stride, qr, kc, vc);
+            if (!gemm(ls.qkv, l, 0, &y, &nz)) return false;
+            k_bd_rope_kv<<<nseq, PF_THREADS, 0, s>>>(y, nz, d_pos, nq, nh, nkv, hd, p->rcos,
+                                                     p->rsin, mp, seq_stride, qr, kc, vc);
             att<<<dim3(nseq, nkv), BD_ATT_THREADS, att_smem, s>>>(
-                qr, kc, vc, d_pos, nh, t.groups, mp, seq_stride, p->scale, cx);
-            if (!gemm(ls.o, l, 1, cx, big)) return false;
-            k_pf_add<<<ew_blocks, 256, 0, s>>>(h, big, (long long)nseq * H, hB);
-            k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(hB, p->dev_norm[2 * l + 1], p->eps[2 * l + 1], H,
-                                                    xn);
-            if (!gemm(ls.gu, l, 2, xn, big)) return false;
-            k_pf_swiglu<<<ew_blocks, 256, 0, s>>>(big, F, (long long)nseq * F, act);
-            if (!gemm(ls.dn, l, 3, act, big)) return false;
-            k_pf_add<<<ew_blocks, 256, 0, s>>>(hB, big, (long long)nseq * H, h);
-            g_launches += 7;
+                qr, kc, vc, d_pos, nh, t.groups, mp, seq_stride, p->scale, lt, xs);
+            if (!gemm(ls.o, l, 1, &y, &nz)) return false;
+            k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(h, nullptr, nullptr, y, nz,
+                                                      p->dev_norm[2 * l + 1], p->eps[2 * l + 1],
+                                                      H, hB, lt, xs);
+            if (!gemm(ls.gu, l, 2, &y, &nz)) return false;
+            k_bd_swiglu<<<ew_blocks, 256, 0, s>>>(y, nz, nseq, F, lt, xs);
+            if (!gemm(ls.dn, l, 3, &y, &nz)) return false;
+            const bool last = l + 1 == L;
+            k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(
+                hB, nullptr, nullptr, y, nz, last ? p->dev_norm.back() : p->dev_norm[2 * l + 2],
+                last ? p->f_eps : p->eps[2 * l + 2], H, h, last ? lmt : lt, xs);
+            g_launches += 5;
         }
-        k_pf_rmsnorm<<<nseq, PF_THREADS, 0, s>>>(h, p->dev_norm.back(), p->f_eps, H, xn);
-        if (!gemm(t.lm, 0, 4, xn, big)) return false;
-        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(big, V, d_start, max_new, d_tok, d_pos, d_gen);
-        g_launches += 3;
+        if (!gemm(t.lm, 0, 4, &y, &nz)) return false;
+        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(y, nz, V, d_start, max_new, d_tok, d_pos, d_gen);
+        g_launches++;
         return KLLM_CUDA(cudaGetLastError());
     };
     bool ok = true;
