@@ -966,6 +966,25 @@ def run_config4(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def c4_profile(new_tokens):
+    """Profiling aid: one config-4 batch (32 sequences x 1024-token prompts)
+    with `new_tokens` generated each; prints the prompt-pass and per-step
+    device times and the launch count (no JSON line)."""
+    import kmap_b200
+    kmap_b200.require_gpu()
+    import torch
+    torch.cuda.set_device(0)
+    path, _ = c4_chip(0)
+    with kmap_b200.Chip(path) as chip:
+        V = chip.info["vocab_size"]
+        rng = np.random.default_rng(11)
+        prompts = [rng.integers(3, V, C4_PROMPT).astype(np.int32) for _ in range(C4_SEQS)]
+        chip.infer_batch(prompts, new_tokens)
+        st = chip.stats()
+    log("c4: prompt passes %.1f ms, %d steps %.3f ms each, %d launches" % (
+        st["prefill_ms"], new_tokens, st["decode_ms"] / new_tokens, st["launches"]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -998,6 +1017,9 @@ def main():
     ap.add_argument("--ttgemm-shape", type=int, nargs=4, metavar=("ROWS", "K", "N", "CODES"),
                     help="profiling aid: time kllm_tt_gemm (prefill TT-GEMM) on one seeded "
                          "shape over --steps launches, beside kllm_tt_gemv, and exit")
+    ap.add_argument("--c4-profile", type=int, metavar="NEW",
+                    help="profiling aid: one 32 x 1024-token batch on the 8B chip with NEW "
+                         "tokens generated each; prints step times and exits")
     ap.add_argument("--ttgemv-shape", type=int, nargs=3, metavar=("K", "N", "CODES"),
                     help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
                          "--steps times and exit (no JSON line)")
@@ -1010,6 +1032,9 @@ def main():
         return
     if args.ttgemm_shape:
         ttgemm_time(*args.ttgemm_shape, reps=args.steps)
+        return
+    if args.c4_profile:
+        c4_profile(args.c4_profile)
         return
     if args.ttgemv_shape:
         ttgemv_once(*args.ttgemv_shape, reps=args.steps)
