@@ -11,12 +11,15 @@
 // in the prompt pass.
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include "common.cuh"
 #include "prefill.cuh"
 
 namespace kllm {
+
+namespace cg = cooperative_groups;
 
 // One element of a GEMM output: the sum of its nz K-range partial tiles,
 // part[z * plane + i], in range order (nz = 1: the output itself).
@@ -48,28 +51,42 @@ __device__ __forceinline__ void bd_emit(float v, size_t i, int terms, size_t pla
 // Row r: x = res[r] + (the GEMM output's row, or nothing when part is
 // null; with res null, the embedding row of tok[r]); hout[r] = x; then
 // the tape's RMSNORM -- sum of squares, mean as sum * (1 / H) + eps, rsqrt
-// in double, two rounded products -- into the next GEMM's input.
-// (grid: nseq blocks, PF_THREADS threads)
-__global__ void k_bd_add_norm(const float *__restrict__ res, const float *__restrict__ embed,
-                              const int *__restrict__ tok, const float *__restrict__ part, int nz,
-                              const float *__restrict__ w, float eps, int H,
-                              float *__restrict__ hout, int terms, void *__restrict__ xs) {
+// in double, two rounded products -- into the next GEMM's input.  A
+// cluster of BD_CL CTAs per row, each a contiguous slice of H: the slices'
+// sums of squares (block sums of a fixed shape) are read from every CTA's
+// shared memory and added in slice order, so all CTAs of the row agree.
+// (grid: nseq * BD_CL blocks, PF_THREADS threads)
+constexpr int BD_CL = 8;
+
+__global__ void __cluster_dims__(BD_CL, 1, 1) __launch_bounds__(PF_THREADS)
+k_bd_add_norm(const float *__restrict__ res, const float *__restrict__ embed,
+              const int *__restrict__ tok, const float *__restrict__ part, int nz,
+              const float *__restrict__ w, float eps, int H, float *__restrict__ hout, int terms,
+              void *__restrict__ xs) {
     __shared__ float red[PF_THREADS / 32];
-    const int r = blockIdx.x;
-    const size_t plane = (size_t)gridDim.x * H;
+    __shared__ float css;
+    cg::cluster_group cl = cg::this_cluster();
+    const int r = blockIdx.x / BD_CL, c = (int)cl.block_rank();
+    const size_t plane = (size_t)(gridDim.x / BD_CL) * H;
+    const int per = (H + BD_CL - 1) / BD_CL, i0 = c * per, i1 = min(H, i0 + per);
     const float *src = res ? res + (size_t)r * H : embed + (size_t)tok[r] * H;
     float *hr = hout + (size_t)r * H;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += PF_THREADS) {
+    for (int i = i0 + threadIdx.x; i < i1; i += PF_THREADS) {
         float v = src[i];
         if (part) v = __fadd_rn(v, bd_sum(part, nz, plane, (size_t)r * H + i));
         hr[i] = v;
         ss = __fadd_rn(ss, __fmul_rn(v, v));
     }
-    const float tot = pf_block_sum(ss, red);
+    const float mine = pf_block_sum(ss, red);
+    if (threadIdx.x == 0) css = mine;
+    cl.sync();
+    float tot = *cl.map_shared_rank(&css, 0);
+    for (int k = 1; k < BD_CL; k++) tot = __fadd_rn(tot, *cl.map_shared_rank(&css, k));
+    cl.sync();   // every CTA has read every slice's sum before any leaves
     const float add = __fadd_rn(__fmul_rn(tot, 1.0f / (float)H), eps);
     const float rsq = (float)(1.0 / sqrt((double)add));
-    for (int i = threadIdx.x; i < H; i += PF_THREADS)   // this thread's own writes above
+    for (int i = i0 + threadIdx.x; i < i1; i += PF_THREADS)   // this thread's own writes above
         bd_emit(__fmul_rn(__fmul_rn(hr[i], rsq), w[i]), (size_t)r * H + i, terms, plane, xs);
 }
 
@@ -92,7 +109,8 @@ __global__ void k_bd_swiglu(const float *__restrict__ part, int nz, int nseq, in
 // Row r of the QKV GEMM output at position pos[r]: rotate-half RoPE of q
 // (to q_out[r]) and k, k and v appended to sequence r's cache (row pos[r]).
 // Caches: [seq][layer][kv_head][max_pos][hd]; kc / vc point at this layer of
-// sequence 0, seq_stride floats apart.  (grid: nseq blocks)
+// sequence 0, seq_stride floats apart.  (grid: nseq x any number of
+// blocks over the row's outputs)
 __global__ void k_bd_rope_kv(const float *__restrict__ part, int nz, const int *__restrict__ pos,
                              int nq, int nh, int nkv, int hd, const float *__restrict__ rcos,
                              const float *__restrict__ rsin, int max_pos, size_t seq_stride,
@@ -102,7 +120,8 @@ __global__ void k_bd_rope_kv(const float *__restrict__ part, int nz, const int *
     const int qd = nh * hd, kvd = nkv * hd;
     const size_t plane = (size_t)gridDim.x * nq, row = (size_t)r * nq;
     float *kr = kc + (size_t)r * seq_stride, *vr = vc + (size_t)r * seq_stride;
-    for (int n = threadIdx.x; n < qd + 2 * kvd; n += blockDim.x) {
+    for (int n = blockIdx.y * blockDim.x + threadIdx.x; n < qd + 2 * kvd;
+         n += gridDim.y * blockDim.x) {
         const float y = bd_sum(part, nz, plane, row + n);
         if (n < qd + kvd) {
             const int head = n / hd, dim = n % hd, half = hd / 2;
@@ -123,12 +142,13 @@ __global__ void k_bd_rope_kv(const float *__restrict__ part, int nz, const int *
 
 // Attention of row r for the `groups` query heads of kv head g at once
 // (each cached k / v row read once): grid nseq x nkv, BD_ATT_THREADS
-// threads.  Scores: warp w takes positions w, w + 8, ...; lane i holds
+// threads (8 warps, 8 rows of each in flight; two CTAs per SM).  Scores:
+// warp w takes positions w, w + 8, ...; lane i holds
 // dims [VEC i, VEC i + VEC) of the row; q.k is the lane's serial sum over
 // its dims, then the xor-shuffle tree over the lanes, times the scale.
 // Softmax of query head j by warp j: max, exp in double of the difference,
 // the lanes' serial sums then the tree, division.  P.V: warp w sums its
-// positions serially per dim, the 8 warps' sums added in warp order, into
+// positions serially per dim, the warps' sums added in warp order, into
 // the O GEMM's input.  Dynamic shared memory: bd_att_smem(groups, HD,
 // max_pos) bytes.
 constexpr int BD_ATT_THREADS = 256;
@@ -152,11 +172,11 @@ __device__ __forceinline__ void bd_load(const float *p, float (&v)[VEC]) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(BD_ATT_THREADS)
+__global__ void __launch_bounds__(BD_ATT_THREADS, 2)
 k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
                 const float *__restrict__ vc, const int *__restrict__ pos, int nh, int groups,
                 int max_pos, size_t seq_stride, float scale, int terms, void *__restrict__ xs) {
-    constexpr int VEC = HD / 32, NW = BD_ATT_THREADS / 32, U = 4, GB = 8;
+    constexpr int VEC = HD / 32, NW = BD_ATT_THREADS / 32, U = 8, GB = 8;
     extern __shared__ float bsm[];
     const int r = blockIdx.x, g = blockIdx.y, n = pos[r] + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -257,22 +277,25 @@ k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
     }
 }
 
-// Greedy pick of row r of the lm_head GEMM output (the reference's: best =
-// logits[0], then strict > over the rest in index order), written as the row's next token and as
-// its generated token pos[r] - start[r]; the row's position advances.
-// (grid: nseq blocks, PF_THREADS threads)
-__global__ void k_bd_argmax(const float *__restrict__ part, int nz, int V,
-                            const int *__restrict__ start, int max_new, int *__restrict__ tok,
-                            int *__restrict__ pos, int *__restrict__ gen) {
+// Greedy pick of row r of the lm_head GEMM output, the reference's rule
+// (best = logits[0], then strict > over the rest in index order: the first
+// maximum; NaN never wins, a NaN at 0 keeps 0).  Stage 1, grid nseq x
+// BD_AC blocks: the first maximum of each contiguous slice of the row
+// (index -1 when the slice has none).
+constexpr int BD_AC = 32;
+
+__global__ void k_bd_argmax_part(const float *__restrict__ part, int nz, int V,
+                                 float *__restrict__ cand_v, int *__restrict__ cand_i) {
     __shared__ float bv[PF_THREADS];
     __shared__ int bi[PF_THREADS];
-    const int r = blockIdx.x;
+    const int r = blockIdx.x, c = blockIdx.y;
     const size_t plane = (size_t)gridDim.x * V, row = (size_t)r * V;
+    const int per = (V + BD_AC - 1) / BD_AC, v0 = c * per, v1 = min(V, v0 + per);
     float best = -INFINITY;
     int idx = -1;
-    for (int v = threadIdx.x; v < V; v += PF_THREADS) {
+    for (int v = v0 + threadIdx.x; v < v1; v += PF_THREADS) {
         const float x = bd_sum(part, nz, plane, row + v);
-        if (x > best) {   // per thread: first maximum in index order (NaN never wins)
+        if (x > best) {   // per thread: first maximum in index order
             best = x;
             idx = v;
         }
@@ -281,20 +304,42 @@ __global__ void k_bd_argmax(const float *__restrict__ part, int nz, int V,
     bi[threadIdx.x] = idx;
     __syncthreads();
     if (threadIdx.x == 0) {
-        float b = bd_sum(part, nz, plane, row);
-        int k = 0;
-        if (!(b != b)) {   // NaN at 0: the reference keeps index 0
-            for (int t = 0; t < PF_THREADS; t++)
-                if (bi[t] >= 0 && (bv[t] > b || (bv[t] == b && bi[t] < k))) {
-                    b = bv[t];
-                    k = bi[t];
-                }
-        }
-        tok[r] = k;
-        const int step = pos[r] - start[r];
-        if (step >= 0 && step < max_new) gen[(size_t)r * max_new + step] = k;
-        pos[r] = pos[r] + 1;
+        float b = -INFINITY;
+        int k = -1;
+        for (int t = 0; t < PF_THREADS; t++)
+            if (bi[t] >= 0 && (k < 0 || bv[t] > b || (bv[t] == b && bi[t] < k))) {
+                b = bv[t];
+                k = bi[t];
+            }
+        cand_v[r * BD_AC + c] = b;
+        cand_i[r * BD_AC + c] = k;
     }
+}
+
+// Stage 2, one thread per row: the slices' maxima in slice order from
+// (logits[0], 0), strict >; written as the row's next token and as its
+// generated token pos[r] - start[r]; the row's position advances.
+__global__ void k_bd_argmax_pick(const float *__restrict__ part, int nz, int V, int nseq,
+                                 const float *__restrict__ cand_v, const int *__restrict__ cand_i,
+                                 const int *__restrict__ start, int max_new,
+                                 int *__restrict__ tok, int *__restrict__ pos,
+                                 int *__restrict__ gen) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= nseq) return;
+    float b = bd_sum(part, nz, (size_t)nseq * V, (size_t)r * V);
+    int k = 0;
+    if (!(b != b))   // NaN at 0: the reference keeps index 0
+        for (int c = 0; c < BD_AC; c++) {
+            const int i = cand_i[r * BD_AC + c];
+            if (i >= 0 && cand_v[r * BD_AC + c] > b) {
+                b = cand_v[r * BD_AC + c];
+                k = i;
+            }
+        }
+    tok[r] = k;
+    const int step = pos[r] - start[r];
+    if (step >= 0 && step < max_new) gen[(size_t)r * max_new + step] = k;
+    pos[r] = pos[r] + 1;
 }
 
 }  // namespace kllm

@@ -1510,17 +1510,18 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
     // arena (floats, each piece a multiple of 4): K and V caches of every
     // sequence; residual rows h, hB [nseq][H]; big [nseq][max(nq, 2F, V)]
     // (a GEMM output in one piece); qr [nseq][qd]; xs, a GEMM's input (fp32
-    // rows or three bf16 terms); split-K partials; ints: prompts, tokens,
-    // positions, first positions, generated tokens
+    // rows or three bf16 terms); split-K partials; the greedy pick's slice
+    // maxima; ints: prompts, tokens, positions, first positions, generated
+    // tokens, the slice maxima's indices
     auto up4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t seq_stride = (size_t)L * nkv * mp * hd;
     const size_t kv = up4((size_t)nseq * seq_stride);
     const size_t rh = up4((size_t)nseq * H), rq = up4((size_t)nseq * qd);
     const size_t wide = up4((size_t)nseq * std::max({(size_t)nq, (size_t)2 * F, (size_t)H, (size_t)V}));
     const size_t rxs = up4(((size_t)3 * nseq * std::max({(size_t)H, (size_t)F, (size_t)qd}) + 1) / 2);
-    const size_t rpart = up4(part_n);
-    const size_t ints = up4(total + 3 * (size_t)nseq + (size_t)nseq * max_new);
-    const size_t need = 2 * kv + 2 * rh + wide + rq + rxs + rpart + ints;
+    const size_t rpart = up4(part_n), rcand = up4((size_t)nseq * BD_AC);
+    const size_t ints = up4(total + 3 * (size_t)nseq + (size_t)nseq * max_new) + rcand;
+    const size_t need = 2 * kv + 2 * rh + wide + rq + rxs + rpart + rcand + ints;
     if (p->bd_cap < need) {
         if (!KLLM_CUDA(cudaStreamSynchronize(s))) return false;
         if (p->bd_arena) cudaFree(p->bd_arena);
@@ -1530,9 +1531,10 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
         p->bd_cap = need;
     }
     float *kcs = p->bd_arena, *vcs = kcs + kv, *h = vcs + kv, *hB = h + rh, *big = hB + rh,
-          *qr = big + wide, *xs = qr + rq, *part = xs + rxs;
-    int *d_prompts = reinterpret_cast<int *>(part + rpart), *d_tok = d_prompts + total,
-        *d_pos = d_tok + nseq, *d_start = d_pos + nseq, *d_gen = d_start + nseq;
+          *qr = big + wide, *xs = qr + rq, *part = xs + rxs, *cand_v = part + rpart;
+    int *d_cand_i = reinterpret_cast<int *>(cand_v + rcand), *d_prompts = d_cand_i + rcand,
+        *d_tok = d_prompts + total, *d_pos = d_tok + nseq, *d_start = d_pos + nseq,
+        *d_gen = d_start + nseq;
     std::vector<int> tok0(nseq), pos0(nseq);
     {
         size_t off = 0;
@@ -1606,33 +1608,35 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
     auto record_step = [&]() -> bool {
         const float *y = nullptr;
         int nz = 1;
-        k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(nullptr, p->embed, d_tok, nullptr, 1,
+        k_bd_add_norm<<<nseq * BD_CL, PF_THREADS, 0, s>>>(nullptr, p->embed, d_tok, nullptr, 1,
                                                   p->dev_norm[0], p->eps[0], H, h, lt, xs);
         g_launches++;
         for (int l = 0; l < L; l++) {
             const LayerSlots &ls = t.layers[l];
             float *kc = kcs + (size_t)l * nkv * mp * hd, *vc = vcs + (size_t)l * nkv * mp * hd;
             if (!gemm(ls.qkv, l, 0, &y, &nz)) return false;
-            k_bd_rope_kv<<<nseq, PF_THREADS, 0, s>>>(y, nz, d_pos, nq, nh, nkv, hd, p->rcos,
+            k_bd_rope_kv<<<dim3(nseq, 8), PF_THREADS, 0, s>>>(y, nz, d_pos, nq, nh, nkv, hd, p->rcos,
                                                      p->rsin, mp, seq_stride, qr, kc, vc);
             att<<<dim3(nseq, nkv), BD_ATT_THREADS, att_smem, s>>>(
                 qr, kc, vc, d_pos, nh, t.groups, mp, seq_stride, p->scale, lt, xs);
             if (!gemm(ls.o, l, 1, &y, &nz)) return false;
-            k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(h, nullptr, nullptr, y, nz,
+            k_bd_add_norm<<<nseq * BD_CL, PF_THREADS, 0, s>>>(h, nullptr, nullptr, y, nz,
                                                       p->dev_norm[2 * l + 1], p->eps[2 * l + 1],
                                                       H, hB, lt, xs);
             if (!gemm(ls.gu, l, 2, &y, &nz)) return false;
             k_bd_swiglu<<<ew_blocks, 256, 0, s>>>(y, nz, nseq, F, lt, xs);
             if (!gemm(ls.dn, l, 3, &y, &nz)) return false;
             const bool last = l + 1 == L;
-            k_bd_add_norm<<<nseq, PF_THREADS, 0, s>>>(
+            k_bd_add_norm<<<nseq * BD_CL, PF_THREADS, 0, s>>>(
                 hB, nullptr, nullptr, y, nz, last ? p->dev_norm.back() : p->dev_norm[2 * l + 2],
                 last ? p->f_eps : p->eps[2 * l + 2], H, h, last ? lmt : lt, xs);
             g_launches += 5;
         }
         if (!gemm(t.lm, 0, 4, &y, &nz)) return false;
-        k_bd_argmax<<<nseq, PF_THREADS, 0, s>>>(y, nz, V, d_start, max_new, d_tok, d_pos, d_gen);
-        g_launches++;
+        k_bd_argmax_part<<<dim3(nseq, BD_AC), PF_THREADS, 0, s>>>(y, nz, V, cand_v, d_cand_i);
+        k_bd_argmax_pick<<<(nseq + 31) / 32, 32, 0, s>>>(y, nz, V, nseq, cand_v, d_cand_i, d_start,
+                                                        max_new, d_tok, d_pos, d_gen);
+        g_launches += 2;
         return KLLM_CUDA(cudaGetLastError());
     };
     bool ok = true;
