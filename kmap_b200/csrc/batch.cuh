@@ -171,7 +171,32 @@ __device__ __forceinline__ void bd_load(const float *p, float (&v)[VEC]) {
     }
 }
 
-template <int HD>
+// Butterfly reduce-scatter over the warp: on return lane l holds the sum
+// over all 32 lanes of v[l % P] (P - 1 shuffles for the low lane bits, one
+// per higher bit), the additions in a fixed order.
+template <int P>
+__device__ __forceinline__ float bd_bfly(float (&v)[P], int lane) {
+#pragma unroll
+    for (int m = P / 2, L = P; m >= 1; m >>= 1, L >>= 1) {
+        const bool up = lane & m;
+#pragma unroll
+        for (int i = 0; i < L / 2; i++) {
+            const float send = up ? v[i] : v[i + L / 2];
+            const float keep = up ? v[i + L / 2] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int m = 16; m >= P; m >>= 1) r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, m));
+    return r;
+}
+
+// G: query heads per kv head when it is 1, 2, 4 or 8 (0: any, read at run
+// time).  With G known, a warp takes U positions at once and all U x G dot
+// products share one butterfly (lane l ends with product l: position l / G,
+// head l % G); otherwise each product has its own xor tree.
+template <int HD, int G>
 __global__ void __launch_bounds__(BD_ATT_THREADS, 2)
 k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
                 const float *__restrict__ vc, const int *__restrict__ pos, int nh, int groups,
@@ -189,6 +214,40 @@ k_bd_attn_group(const float *__restrict__ q, const float *__restrict__ kc,
     const float *vg = vc + (size_t)r * seq_stride + (size_t)g * max_pos * HD + VEC * lane;
     for (int i = threadIdx.x; i < groups * HD; i += BD_ATT_THREADS) qs[i] = qrow[i];
     __syncthreads();
+    if constexpr (G > 0) {
+        constexpr int UG = 32 / G < 32 / VEC ? 32 / G : 32 / VEC, P = UG * G;
+        float qv[G][VEC];
+#pragma unroll
+        for (int hq = 0; hq < G; hq++)
+#pragma unroll
+            for (int e = 0; e < VEC; e++) qv[hq][e] = qs[hq * HD + VEC * lane + e];
+        for (int j0 = warp; j0 < n; j0 += UG * NW) {
+            float kv[UG][VEC];
+#pragma unroll
+            for (int u = 0; u < UG; u++) {
+                const int j = j0 + u * NW;
+                if (j < n) {
+                    bd_load<VEC>(kg + (size_t)j * HD, kv[u]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < VEC; e++) kv[u][e] = 0.f;
+                }
+            }
+            float v[P];
+#pragma unroll
+            for (int u = 0; u < UG; u++)
+#pragma unroll
+                for (int hq = 0; hq < G; hq++) {
+                    float d = 0.f;
+#pragma unroll
+                    for (int e = 0; e < VEC; e++) d = __fadd_rn(d, __fmul_rn(qv[hq][e], kv[u][e]));
+                    v[u * G + hq] = d;
+                }
+            const float tot = bd_bfly<P>(v, lane);
+            const int j = j0 + (lane / G) * NW;
+            if (lane < P && j < n) sc[(size_t)(lane % G) * max_pos + j] = __fmul_rn(tot, scale);
+        }
+    } else
     // scores: U positions of this warp in flight at a time
     for (int j0 = warp; j0 < n; j0 += U * NW) {
         float kv[U][VEC];

@@ -30,6 +30,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <chrono>
 #include <set>
 #include <vector>
@@ -1594,8 +1595,15 @@ bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq,
     const int lt = layer_tc ? 3 : 0, lmt = lm_tc ? 3 : 0;
     if (tc && !bd_gemm_prepare()) return false;
     const int ew_blocks = 148 * 8;
-    auto att = hd == 32 ? k_bd_attn_group<32> : hd == 64 ? k_bd_attn_group<64>
-                                                         : k_bd_attn_group<128>;
+    auto att_for = [](auto hdc, int groups) {
+        constexpr int D = decltype(hdc)::value;
+        return groups == 1 ? k_bd_attn_group<D, 1> : groups == 2 ? k_bd_attn_group<D, 2>
+             : groups == 4 ? k_bd_attn_group<D, 4> : groups == 8 ? k_bd_attn_group<D, 8>
+                           : k_bd_attn_group<D, 0>;
+    };
+    auto att = hd == 32 ? att_for(std::integral_constant<int, 32>(), t.groups)
+             : hd == 64 ? att_for(std::integral_constant<int, 64>(), t.groups)
+                        : att_for(std::integral_constant<int, 128>(), t.groups);
     if (att_smem > 48 * 1024 &&
         !KLLM_CUDA(cudaFuncSetAttribute(att, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)att_smem)))
