@@ -71,7 +71,7 @@ def peaks():
         return {}
 
 
-def config0_chip(rank=0, layers=None):
+def tinyllama_chip(rank=0, layers=None):
     spec = chipgen.ModelSpec(**{**chipgen.TINYLLAMA_1B.__dict__})
     spec.max_seq = 2048
     if layers:
@@ -137,7 +137,7 @@ class Clocks:
 # ------------------------------------------------------------ roofline ---
 
 def ttgemv_roofline(device_index):
-    """Average launch time of the TT-GEMV on the config-1 shapes, timed with
+    """Average launch time of the TT-GEMV on the benchmark shapes (TT_SHAPES), timed with
     CUDA events on the launching stream; copies rotate so that every launch
     reads its indices from HBM.  `us`: one launch per copy captured in a CUDA
     graph and replayed, so the kernels run back to back (the device time of
@@ -205,7 +205,7 @@ def ttgemv_roofline(device_index):
 
 
 def ttgemv_once(K, N, C, reps):
-    """kllm_tt_gemv on one seeded config-1 shape, `reps` launches (for ncu)."""
+    """kllm_tt_gemv on one seeded benchmark shape, `reps` launches (for ncu)."""
     import torch
 
     import kmap_b200
@@ -271,7 +271,7 @@ REF_CORES = 8   # the reference's TT pool is 8 threads (compile-time fixed)
 
 
 def prefill_measure(path, reps=3):
-    """Config-2 workload on the config-0 chip: a 2047-token uniform-random
+    """The 2047-token prompt on the TinyLlama-arch chip: a uniform-random
     prompt (the chip's 2048 positions less the first generated token), batch
     1.  Device time of the prompt pass -- the batched pass (TT-GEMMs and row
     kernels for positions 0..2045, then position 2046 as a decode step) and
@@ -307,7 +307,7 @@ def prefill_run(steps, warmup):
     """The prefill measurement alone, as one JSON line."""
     import kmap_b200
     kmap_b200.require_gpu()
-    r = prefill_measure(config0_chip(0), reps=max(steps, 1))
+    r = prefill_measure(tinyllama_chip(0), reps=max(steps, 1))
     print(json.dumps({"metric": "prefill tok/s (prompt positions per second, device time)",
                       "value": r["value"], "unit": "tok/s", "n_gpus": 1, "steps": steps,
                       "warmup": warmup, "higher_is_better": True, "data": "synthetic",
@@ -346,12 +346,12 @@ def pin_reference_cores():
 
 def cpu_sample(out_path):
     """Child process of the GPU arm: the compiled reference runtime on
-    REF_CORES pinned host cores, the whole config-0 call (32 prompt + 128
+    REF_CORES pinned host cores, the whole TinyLlama-arch call (32 prompt + 128
     greedy positions) once, with every position's logits; writes an npz."""
     cores = pin_reference_cores()
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import harness
-    chip = config0_chip()
+    chip = tinyllama_chip()
     ref = harness.Ref()
     h, info = ref.chip(chip)
     p = prompt_ids()
@@ -389,7 +389,7 @@ def decode_small(layers, steps, warmup):
     """Decode PROMPT + 16 tokens on a reduced-depth TinyLlama-width chip."""
     import kmap_b200
     kmap_b200.require_gpu()
-    chip = kmap_b200.Chip(config0_chip(0, layers))
+    chip = kmap_b200.Chip(tinyllama_chip(0, layers))
     p = prompt_ids()
     for _ in range(max(warmup, 1)):
         chip.infer(p, 16)
@@ -408,7 +408,7 @@ REF_WINDOW = 8   # tape positions per reference-arm step
 
 def run_reference_arm(args, rank, world):
     """The compiled reference runtime on REF_CORES pinned host cores.  Each
-    step runs the next REF_WINDOW positions of the config-0 call (32 prompt +
+    step runs the next REF_WINDOW positions of the TinyLlama-arch call (32 prompt +
     128 greedy positions, the reference's own greedy loop), so 20 steps time
     exactly one whole call; a new call starts after position 159."""
     if rank != 0:
@@ -420,7 +420,7 @@ def run_reference_arm(args, rank, world):
                           "the reference runtime was not compiled into oracle/_ref"}))
         return
     cores = pin_reference_cores()
-    chip = config0_chip()
+    chip = tinyllama_chip()
     ref = harness.Ref()
     h, info = ref.chip(chip)
     p = prompt_ids()
@@ -494,7 +494,7 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
-    chip_path = config0_chip(rank)
+    chip_path = tinyllama_chip(rank)
     order = kmap_b200.ORDER_FAST if args.order == "fast" else kmap_b200.ORDER_EXACT
     t_open = time.time()
     chip = kmap_b200.Chip(chip_path, order=order)
@@ -672,13 +672,13 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-# ------------------------------------------------- config 3 (7B, decode) --
+# --------------------------------------------------------- 7B-arch decode --
 
-C3_PROMPT, C3_GEN = 4096, 256
-C3_INDEX_BYTES = 13214154752   # sum of K * N * 2 over the 7B chip's 129 TT matrices
+L7B_PROMPT, L7B_GEN = 4096, 256
+L7B_INDEX_BYTES = 13214154752   # sum of K * N * 2 over the 7B chip's 129 TT matrices
 
 
-def c3_chip(local_rank):
+def chip_7b(local_rank):
     """The Llama-2-7B-architecture chip (32 x 4096, 32 MHA heads of 128,
     SwiGLU 11008, vocab 32000, max_seq 4352), weights drawn on the GPU."""
     import fcntl
@@ -694,8 +694,8 @@ def c3_chip(local_rank):
     return path
 
 
-def run_config3(args, rank, world, local_rank):
-    """Config 3: batch-1 greedy decode of 256 tokens after a 4096-token
+def run_7b(args, rank, world, local_rank):
+    """7B-arch decode: batch-1 greedy decode of 256 tokens after a 4096-token
     uniform-random prompt on the 7B-architecture chip; the prompt through
     the batched pass (tensor-core projections), then one decode step kernel
     per token, column-sharded over the N GPUs for N > 1.  value = generated
@@ -714,7 +714,7 @@ def run_config3(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local_rank))
-    path = c3_chip(local_rank)
+    path = chip_7b(local_rank)
     if dist:
         dist.barrier()
     t_open = time.time()
@@ -728,12 +728,12 @@ def run_config3(args, rank, world, local_rank):
     short = np.random.default_rng(5).integers(3, V, 16).astype(np.int32)
     toks_short = chip.infer(short, 8)
     lg_short = chip.final_logits()
-    prompt = np.random.default_rng(3).integers(3, V, C3_PROMPT).astype(np.int32)
+    prompt = np.random.default_rng(3).integers(3, V, L7B_PROMPT).astype(np.int32)
     t0 = time.time()
-    chip.infer(prompt, C3_GEN)
+    chip.infer(prompt, L7B_GEN)
     t_first = time.time() - t0
     for _ in range(max(args.warmup - 1, 0)):
-        chip.infer(prompt, C3_GEN)
+        chip.infer(prompt, L7B_GEN)
 
     def barrier():
         if dist:
@@ -744,7 +744,7 @@ def run_config3(args, rank, world, local_rank):
     pre_ms, dec_ms, gen = 0.0, 0.0, 0
     with Clocks(local_rank) as clk:
         for _ in range(args.steps):
-            toks = chip.infer(prompt, C3_GEN)
+            toks = chip.infer(prompt, L7B_GEN)
             st = chip.stats()
             pre_ms += st["prefill_ms"]
             dec_ms += st["decode_ms"]
@@ -761,9 +761,9 @@ def run_config3(args, rank, world, local_rank):
         return
     # decode_ms covers the 256 generated tokens' steps after the prompt's
     # last position (plus the final fed token): one kernel per step
-    steps_dec = C3_GEN
+    steps_dec = L7B_GEN
     step_us = dec_ms * 1e3 / (args.steps * steps_dec)
-    gbs = C3_INDEX_BYTES / (step_us * 1e-6) / 1e9
+    gbs = L7B_INDEX_BYTES / (step_us * 1e-6) / 1e9
     hbm = peaks().get("hbm_gbs")
     out = {"metric": "decode tok/s (generated tokens per second of decode device time)",
            "value": gen / (dec_ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -774,10 +774,10 @@ def run_config3(args, rank, world, local_rank):
                       "4096-token prompt + 256 greedy tokens, batch 1",
                       "parallelism": ("column-sharded over %d GPUs" % world if world > 1
                                       else "single GPU")},
-           "prefill": {"tok_s": args.steps * (C3_PROMPT - 1) / (pre_ms / 1e3),
+           "prefill": {"tok_s": args.steps * (L7B_PROMPT - 1) / (pre_ms / 1e3),
                        "ms_per_prompt": pre_ms / args.steps},
            "roofline": {"bound": "hbm", "kernel": "k_decode_step", "launch_us": step_us,
-                        "algorithmic_bytes_per_launch": C3_INDEX_BYTES, "achieved": gbs,
+                        "algorithmic_bytes_per_launch": L7B_INDEX_BYTES, "achieved": gbs,
                         "peak": hbm * world if hbm else None, "unit": "GB/s",
                         "frac": gbs / (hbm * world) if hbm else None},
            "load": {"chip_open_s": t_open, "first_call_s": t_first},
@@ -806,10 +806,10 @@ def run_config3(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-C4_SEQS, C4_PROMPT, C4_GEN = 32, 1024, 128
+B8_SEQS, B8_PROMPT, B8_GEN = 32, 1024, 128
 
 
-def c4_chip(local_rank):
+def chip_8b(local_rank):
     """The Llama-3-8B-architecture chip (32 x 4096, 32 query / 8 kv heads of
     128, SwiGLU 14336, vocab 128256, rope theta 5e5, max_seq 1152), weights
     drawn on the GPU."""
@@ -826,8 +826,8 @@ def c4_chip(local_rank):
     return path, spec
 
 
-def run_config4(args, rank, world, local_rank):
-    """Config 4: greedy decode of 32 concurrent sequences (1024-token
+def run_8b_batch(args, rank, world, local_rank):
+    """8B-arch batched decode: greedy decode of 32 concurrent sequences (1024-token
     uniform-random prompts, 128 generated tokens each) on the
     Llama-3-8B-architecture chip.  Each sequence's prompt goes through the
     batched prompt pass into its own KV cache; every decode step then runs
@@ -853,7 +853,7 @@ def run_config4(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local_rank))
-    path, spec = c4_chip(local_rank)
+    path, spec = chip_8b(local_rank)
     if dist:
         dist.barrier()
     t_open = time.time()
@@ -861,7 +861,7 @@ def run_config4(args, rank, world, local_rank):
     t_open = time.time() - t_open
     V = chip.info["vocab_size"]
     rng = np.random.default_rng(11)
-    prompts = [rng.integers(3, V, C4_PROMPT).astype(np.int32) for _ in range(C4_SEQS)]
+    prompts = [rng.integers(3, V, B8_PROMPT).astype(np.int32) for _ in range(B8_SEQS)]
     mine = prompts[rank::world]
     # parity first: short prompts, batch vs one sequence at a time
     srng = np.random.default_rng(12)
@@ -871,7 +871,7 @@ def run_config4(args, rank, world, local_rank):
     t_first = time.time() - t0
     singles = [chip.infer(p, 8) for p in short]
     for _ in range(args.warmup):
-        chip.infer_batch(mine, C4_GEN)
+        chip.infer_batch(mine, B8_GEN)
 
     def barrier():
         if dist:
@@ -883,7 +883,7 @@ def run_config4(args, rank, world, local_rank):
     with Clocks(local_rank) as clk:
         for _ in range(args.steps):
             t = time.time()
-            outs = chip.infer_batch(mine, C4_GEN)
+            outs = chip.infer_batch(mine, B8_GEN)
             wall += time.time() - t
             st = chip.stats()
             pre_ms += st["prefill_ms"]
@@ -909,10 +909,10 @@ def run_config4(args, rank, world, local_rank):
     kvd = spec.num_key_value_heads * hd
     w_bytes = 2 * (L * (H * (H + 2 * kvd) + H * H + H * 2 * F + F * H) + H * Vv)
     # k and v rows read per step, summed over the steps (n = pos + 1 per row)
-    kv_rows = C4_SEQS * sum(C4_PROMPT + i for i in range(C4_GEN))
+    kv_rows = B8_SEQS * sum(B8_PROMPT + i for i in range(B8_GEN))
     kv_bytes = kv_rows * L * kvd * 4 * 2
-    step_bytes = w_bytes + kv_bytes / C4_GEN
-    step_us = dec_ms * 1e3 / (args.steps * C4_GEN)
+    step_bytes = w_bytes + kv_bytes / B8_GEN
+    step_us = dec_ms * 1e3 / (args.steps * B8_GEN)
     gbs = step_bytes / (step_us * 1e-6) / 1e9
     hbm = peaks().get("hbm_gbs")
     out = {"metric": "batched decode tok/s (generated tokens per second of decode device "
@@ -929,16 +929,16 @@ def run_config4(args, rank, world, local_rank):
                                       else "single GPU"),
                       "l2": "weights 15 GB and caches 9 GB per step exceed L2"},
            "e2e": {"value": gen / wall, "unit": "tok/s",
-                   "h2d_bytes_per_step": 4 * C4_SEQS * C4_PROMPT,
-                   "d2h_bytes_per_step": 4 * C4_SEQS * C4_GEN,
+                   "h2d_bytes_per_step": 4 * B8_SEQS * B8_PROMPT,
+                   "d2h_bytes_per_step": 4 * B8_SEQS * B8_GEN,
                    "note": "wall time of kllm_chip_infer_batch: prompt passes included"},
-           "prefill": {"tok_s": args.steps * C4_SEQS * (C4_PROMPT - 1) / (pre_ms / 1e3),
+           "prefill": {"tok_s": args.steps * B8_SEQS * (B8_PROMPT - 1) / (pre_ms / 1e3),
                        "ms_per_batch": pre_ms / args.steps},
            "roofline": {"bound": "hbm", "kernel": "one decode step of 32 sequences "
                         "(graph: skinny tcgen05 GEMMs, grouped attention, row kernels)",
                         "launch_us": step_us,
                         "algorithmic_bytes_per_launch": step_bytes,
-                        "weight_bytes": w_bytes, "kv_bytes_mean": kv_bytes / C4_GEN,
+                        "weight_bytes": w_bytes, "kv_bytes_mean": kv_bytes / B8_GEN,
                         "achieved": gbs, "peak": hbm * world if hbm else None, "unit": "GB/s",
                         "frac": gbs / (hbm * world) if hbm else None},
            "gpu_launches": launches,
@@ -966,19 +966,19 @@ def run_config4(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def c4_profile(new_tokens):
-    """Profiling aid: one config-4 batch (32 sequences x 1024-token prompts)
+def batch_profile(new_tokens):
+    """Profiling aid: one 8B-arch batch (32 sequences x 1024-token prompts)
     with `new_tokens` generated each; prints the prompt-pass and per-step
     device times and the launch count (no JSON line)."""
     import kmap_b200
     kmap_b200.require_gpu()
     import torch
     torch.cuda.set_device(0)
-    path, _ = c4_chip(0)
+    path, _ = chip_8b(0)
     with kmap_b200.Chip(path) as chip:
         V = chip.info["vocab_size"]
         rng = np.random.default_rng(11)
-        prompts = [rng.integers(3, V, C4_PROMPT).astype(np.int32) for _ in range(C4_SEQS)]
+        prompts = [rng.integers(3, V, B8_PROMPT).astype(np.int32) for _ in range(B8_SEQS)]
         chip.infer_batch(prompts, new_tokens)
         st = chip.stats()
     log("c4: prompt passes %.1f ms, %d steps %.3f ms each, %d launches" % (
@@ -1012,16 +1012,16 @@ def main():
                          "layers (small enough for a profiler), print ms per tape step, "
                          "exit (no JSON line)")
     ap.add_argument("--prefill", action="store_true",
-                    help="config-2 workload: time a 2047-token prompt, batched prompt pass "
+                    help="the 2047-token prompt workload: time it through the batched prompt pass "
                          "beside step by step, print one JSON line and exit")
     ap.add_argument("--ttgemm-shape", type=int, nargs=4, metavar=("ROWS", "K", "N", "CODES"),
                     help="profiling aid: time kllm_tt_gemm (prefill TT-GEMM) on one seeded "
                          "shape over --steps launches, beside kllm_tt_gemv, and exit")
-    ap.add_argument("--c4-profile", type=int, metavar="NEW",
+    ap.add_argument("--batch-profile", type=int, metavar="NEW",
                     help="profiling aid: one 32 x 1024-token batch on the 8B chip with NEW "
                          "tokens generated each; prints step times and exits")
     ap.add_argument("--ttgemv-shape", type=int, nargs=3, metavar=("K", "N", "CODES"),
-                    help="profiling aid: run kllm_tt_gemv on one seeded config-1 shape "
+                    help="profiling aid: run kllm_tt_gemv on one seeded benchmark shape "
                          "--steps times and exit (no JSON line)")
     args = ap.parse_args()
     if args.cpu_sample:
@@ -1033,8 +1033,8 @@ def main():
     if args.ttgemm_shape:
         ttgemm_time(*args.ttgemm_shape, reps=args.steps)
         return
-    if args.c4_profile:
-        c4_profile(args.c4_profile)
+    if args.batch_profile:
+        batch_profile(args.batch_profile)
         return
     if args.ttgemv_shape:
         ttgemv_once(*args.ttgemv_shape, reps=args.steps)
@@ -1046,9 +1046,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.model == "llama2-7b":
-        run_config3(args, rank, world, local_rank)
+        run_7b(args, rank, world, local_rank)
     elif args.model == "llama3-8b-batch":
-        run_config4(args, rank, world, local_rank)
+        run_8b_batch(args, rank, world, local_rank)
     elif args.impl == "reference":
         run_reference_arm(args, rank, world)
     else:
