@@ -62,7 +62,9 @@ enum {
                                result is bit-identical to _tape_runner.c's */
     KLLM_ORDER_FAST = 1     /* K split finer across warps (decode only): same
                                tokens and logits within the decode tolerance,
-                               more parallelism in the narrow projections */
+                               more parallelism in the narrow projections; one
+                               GPU only (a column-sharded context builds the
+                               exact order) */
 };
 
 typedef struct {
