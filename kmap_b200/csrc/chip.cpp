@@ -287,7 +287,7 @@ kllm_chip *kllm_chip_open(const char *dir_c) {
             }
             snprintf(name, sizeof name, "const_%d_indices.bin", s);
             uint16_t *ix = nullptr;
-            if (K * N) {   // mapped, not read: the upload copies it to HBM once
+            if (K > 0 && N > 0) {   // mapped, not read: the upload copies it to HBM once
                 ix = (uint16_t *)map_file(circ + name, K * N * 2, c->maps);
                 if (!ix) return fail();
             } else {
