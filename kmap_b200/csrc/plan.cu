@@ -1442,12 +1442,15 @@ static bool plan_prefill(CtxImpl *c, DecodePlan *p, int R, const int *prompt_dev
 // its last position goes through the batched prompt pass into the
 // sequence's own KV cache; then every step feeds one token per sequence:
 // embedding rows, per layer row RMSNorm, the QKV / O / gate_up / down
-// projections as one TT-GEMM over the nseq rows (each row bit-identical to
-// the TT-GEMV, or on the tensor cores with KLLM_BATCH_TC=1), RoPE and the
-// append at each row's own position, attention over each row's own cache,
-// residual adds and SwiGLU; final norm, lm_head, the first-maximum pick per
-// row.  Sequences run the full max_new steps; out_lens cut each at its
-// first EOS (the reference stops there and emits nothing after it).
+// projections as one GEMM over the nseq rows (the few-row tensor-core GEMM
+// where the codebooks hold bf16 numbers, up to 128 rows; the exact TT-GEMM,
+// each row bit-identical to the TT-GEMV, otherwise or with
+// KLLM_BATCH_TC=0), RoPE and the append at each row's own position,
+// attention over each row's own cache, residual adds and SwiGLU (batch.cuh);
+// final norm, lm_head, the first-maximum pick per row.  One step is
+// captured as a CUDA graph and replayed.  Sequences run the full max_new
+// steps; out_lens cut each at its first EOS (the reference stops there and
+// emits nothing after it).
 bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq, int max_new,
                       int eos, int *out, int *out_lens, double *prefill_ms, double *decode_ms) {
     DecodePlan *p = c->plan;

@@ -41,7 +41,8 @@ bool plan_infer(CtxImpl *c, const int *prompt, int prompt_len, int max_new, int 
 
 // Batched greedy decode of nseq sequences (prompts concatenated, lens[i]
 // tokens each): out[i * max_new + j] is sequence i's token j, out_lens[i]
-// the count before its first EOS.  One GPU, persistent plan prepared.
+// the count before its first EOS.  One GPU, persistent plan prepared;
+// prefill_ms / decode_ms: device time of the prompt passes and the steps.
 bool plan_infer_batch(CtxImpl *c, const int *prompts, const int *lens, int nseq, int max_new,
                       int eos, int *out, int *out_lens, double *prefill_ms, double *decode_ms);
 
