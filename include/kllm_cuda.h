@@ -229,11 +229,13 @@ int kllm_chip_infer(kllm_chip *chip, const int *prompt, int prompt_len, int max_
  * nseq x max_new tokens (row i: sequence i's greedy tokens, computed for all
  * max_new steps), out_lens[i] the number before sequence i's first `eos`
  * (the reference would stop there; pass -1 for none).  Prompts go through
- * the batched prompt pass, then each step is one TT-GEMM per projection
- * over the nseq rows, each row bit-identical to the TT-GEMV (with
- * KLLM_BATCH_TC=1: the tensor-core GEMM, a tolerance result).  The context
- * must not be column-sharded.  Returns 0 or non-zero (kllm_last_error);
- * kllm_get_infer_stats gives the prompt and decode device times. */
+ * the batched prompt pass, then each step is one GEMM per projection over
+ * the nseq rows: on the tensor cores when every codebook entry is a bf16
+ * number and nseq <= 128 (a tolerance result), else -- or with
+ * KLLM_BATCH_TC=0 in the environment -- the exact TT-GEMM, each row
+ * bit-identical to the TT-GEMV.  The context must not be column-sharded.
+ * Returns 0 or non-zero (kllm_last_error); kllm_get_infer_stats gives the
+ * prompt and decode device times. */
 int kllm_infer_batch(TapeCtx *ctx, const int *prompts, const int *prompt_lens, int nseq,
                      int max_new, int eos, int *out, int *out_lens);
 /* The same on a loaded chip (prepares its fused plan first). */
