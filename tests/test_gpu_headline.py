@@ -18,7 +18,6 @@ import os
 import numpy as np
 import pytest
 
-import harness
 
 pytestmark = pytest.mark.gpu
 

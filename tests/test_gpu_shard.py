@@ -14,7 +14,6 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-import harness
 
 pytestmark = pytest.mark.gpu
 
